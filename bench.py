@@ -1,0 +1,406 @@
+"""Benchmark of the LUMA optimizer step on B200 (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl luma|reference]
+                    [--config llama8b|gpt2|ragged|cpu21m]
+
+A "step" is one ``LUMA.step()`` over every parameter tensor of the workload
+(two kernel launches).  Default workload: Llama-3-8B parameter shapes (291
+tensors, 8,030,261,248 params), bf16 params, bf16 grads N(0, 1e-3) drawn once
+before timing (as the reference's bench_compile.py times ``opt.step()`` with
+grads pre-made).  Params, grads and codes are resident in HBM (64 GB), far
+larger than L2, so no L2 flush is needed between steps.
+
+Printed (rank 0, one JSON line): step throughput in Gparams/s (``value``),
+achieved HBM bandwidth against the algorithmic bytes per param, the roofline
+of the dominant kernel (pass 2) from per-pass CUDA events, ``e2e`` through the
+public API with grads copied from pinned host memory every step, the
+reference CPU implementation (oracle restatement of the reference's PyTorch
+backend) timed on this host's cores, and the SM clocks sampled during timing.
+
+``--impl reference`` times the reference algorithm on the host CPU cores
+(the oracle restatement; the reference itself is a Python package that is
+not present on the GPU host) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "LUMA step Gparams/s & HBM GB/s (% of peak), Llama-3-8B shapes, 1/2/4/8 GPU"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# workloads (SURVEY-listed synthetic configs)
+# ---------------------------------------------------------------------------
+
+def llama3_8b_shapes():
+    d, kv, ffn, vocab, layers = 4096, 1024, 14336, 128256, 32
+    shapes = [(vocab, d)]
+    for _ in range(layers):
+        shapes += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
+    shapes += [(d,), (vocab, d)]
+    return shapes
+
+
+def gpt2_small_shapes():
+    d, vocab, ctx = 768, 50257, 1024
+    shapes = [(vocab, d), (ctx, d)]
+    for _ in range(12):
+        shapes += [(d,), (d,), (d, 3 * d), (3 * d,), (d, d), (d,), (d,), (d,),
+                   (d, 4 * d), (4 * d,), (4 * d, d), (d,)]
+    shapes += [(d,), (d,)]
+    return shapes
+
+
+def ragged_shapes(n=10_000, seed=0):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return [(max(1, int(round(2 ** rng.uniform(0, 20)))),) for _ in range(n)]
+
+
+def cpu21m_shapes():
+    return [(1024, 1024)] * 4 + [(4096, 1024)] * 2 + [(1024, 4096)] * 2
+
+
+CONFIGS = {
+    "llama8b": dict(shapes=llama3_8b_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
+                    gscale=1e-3, name="Llama-3-8B shapes (291 tensors), bf16 params, bf16 grads"),
+    "gpt2": dict(shapes=gpt2_small_shapes, pdt=torch.float32, gdt=torch.bfloat16,
+                 gscale=1e-3, name="GPT-2 small shapes (148 tensors), fp32 params, bf16 grads"),
+    "ragged": dict(shapes=ragged_shapes, pdt=torch.float32, gdt=torch.float32,
+                   gscale=1e-2, name="ragged: 10,000 fp32 tensors, numel log-uniform in [1, 2^20]"),
+    "cpu21m": dict(shapes=cpu21m_shapes, pdt=torch.float32, gdt=torch.float32,
+                   gscale=1e-2, name="8 fp32 tensors, 20,971,520 params (reference CPU config)"),
+}
+
+
+def numel(shape):
+    return math.prod(shape) if shape else 1
+
+
+def bytes_per_param(pdt, gdt):
+    """Algorithmic HBM bytes per param per step: pass 1 reads g, Q_m, Q_w;
+    pass 2 reads g, Q_m, Q_w, p and writes p, Q_m, Q_w."""
+    g, p = torch.tensor([], dtype=gdt).element_size(), torch.tensor([], dtype=pdt).element_size()
+    pass1 = g + 4
+    pass2 = g + 4 + 2 * p + 4
+    return pass1, pass2
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(config):
+    """ncu-measured DRAM bytes per param of pass 2, from the committed profile summary."""
+    path = os.path.join(ROOT, "profiles", f"luma_pass2_{config}.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["dram_bytes_per_param"])
+    except Exception:  # noqa: BLE001
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 8:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[4 + k] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference algorithm (oracle restatement) on host cores
+# ---------------------------------------------------------------------------
+
+def cpu_sample_shapes(config):
+    if config == "llama8b":
+        d, kv = 4096, 1024
+        return [(d, d), (kv, d), (kv, d), (d, d)], "one Llama-3-8B attention block: q,k,v,o (33,554,432 params)"
+    if config == "cpu21m":
+        return cpu21m_shapes(), "the full 8-tensor config (20,971,520 params)"
+    if config == "gpt2":
+        d = 768
+        return [(d, 3 * d), (3 * d,), (d, d), (d, 4 * d), (4 * d, d)], "one GPT-2 block's matrices"
+    return ragged_shapes(200, seed=1), "200 ragged tensors"
+
+
+def cpu_baseline(config, steps, warmup, budget_s=20.0):
+    """Gparams/s of the reference algorithm on CPU (torch CPU kernels, all host threads)."""
+    from oracle import philox  # noqa: F401  (test infrastructure: CPU baseline leg)
+    from oracle.luma_ref import OracleLUMA
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    cfg = CONFIGS[config]
+    shapes, sample = cpu_sample_shapes(config)
+    g = torch.Generator().manual_seed(0)
+    params = [(torch.randn(s, generator=g) * 0.02).to(cfg["pdt"]) for s in shapes]
+    grads = [(torch.randn(s, generator=g) * cfg["gscale"]).to(cfg["gdt"]) for s in shapes]
+    for p, gr in zip(params, grads):
+        p.grad_dtype = None
+        p.grad = gr
+    rand_cache = {}
+
+    def draws(pid, t, like):
+        if pid not in rand_cache:
+            rand_cache[pid] = (torch.rand(like.shape, generator=g), torch.rand(like.shape, generator=g))
+        return rand_cache[pid]
+
+    opt = OracleLUMA(params, lr=1e-3, draws=draws)
+    n = sum(numel(s) for s in shapes)
+    for _ in range(max(warmup, 2)):
+        opt.step()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < steps and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        opt.step()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(n / t / 1e9, 6), "unit": "Gparams/s", "cores": cores,
+            "kind": "port", "steps_timed": len(times),
+            "sample": f"{sample}; {cfg['pdt']} params, {cfg['gdt']} grads; median of "
+                      f"{len(times)} steps after {max(warmup, 2)} warm-up; reference "
+                      f"PyTorch-backend op sequence (oracle/luma_ref.py) on CPU tensors"}
+
+
+# ---------------------------------------------------------------------------
+# the CUDA step
+# ---------------------------------------------------------------------------
+
+def make_workload(config, device, seed=0):
+    cfg = CONFIGS[config]
+    shapes = cfg["shapes"]()
+    gen = torch.Generator(device=device).manual_seed(seed)
+    params, grads = [], []
+    for s in shapes:
+        p = torch.empty(s, dtype=cfg["pdt"], device=device)
+        p.normal_(0.0, 0.02, generator=gen)
+        gr = torch.empty(s, dtype=cfg["gdt"], device=device)
+        gr.normal_(0.0, cfg["gscale"], generator=gen)
+        p.grad_dtype = None
+        p.grad = gr
+        params.append(p)
+        grads.append(gr)
+    return shapes, params, grads
+
+
+def run_luma(args, rank, world, local_rank):
+    from luma_b200 import LUMA
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    cfg = CONFIGS[args.config]
+    shapes, params, grads = make_workload(args.config, device)
+    n_params = sum(numel(s) for s in shapes)
+    opt = LUMA(params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    warmup = max(args.warmup, 1)
+    for _ in range(warmup):
+        opt.step()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    stream = torch.cuda.current_stream()
+    for trio in evs:
+        for e in trio:
+            e.record(stream)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    start.record(stream)
+    for k in range(K):
+        opt._step_events = tuple(e.cuda_event for e in evs[k])
+        opt.step()
+    stop.record(stream)
+    torch.cuda.synchronize()
+    opt._step_events = None
+    clocks = sampler.stop()
+    if world > 1:
+        torch.distributed.barrier()
+    total_ms = start.elapsed_time(stop)
+    p1 = [evs[k][0].elapsed_time(evs[k][1]) for k in range(K)]
+    p2 = [evs[k][1].elapsed_time(evs[k][2]) for k in range(K)]
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / K
+
+    # e2e: grads from pinned host memory each step, step through the public
+    # API, read the new per-tensor scales back.
+    e2e = None
+    if not args.no_e2e:
+        try:
+            host = [torch.empty(g.shape, dtype=g.dtype, pin_memory=True) for g in grads]
+            for h, g in zip(host, grads):
+                h.copy_(g)
+            h2d = sum(h.numel() * h.element_size() for h in host)
+            eng = next(iter(opt._engines.values()))
+            d2h = eng.slots.numel()
+            E = max(2, min(K, 5))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(E):
+                for h, g in zip(host, grads):
+                    g.copy_(h, non_blocking=True)
+                opt.step()
+                eng.read_slots()  # D2H of S_m/S_v of every tensor (synchronises)
+            el = time.perf_counter() - t0
+            e2e = {"value": round(n_params * E / el / 1e9, 3), "unit": "Gparams/s",
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": E}
+            del host
+        except Exception as exc:  # noqa: BLE001
+            e2e = {"value": None, "unit": "Gparams/s", "error": str(exc)[:200]}
+
+    p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
+    peak, peak_kind = measured_peak()
+    p2_ms = statistics.mean(p2)
+    achieved = n_params * p2b / (p2_ms * 1e-3) / 1e9
+    traffic_pp = committed_traffic(args.config)
+    return {
+        "n_params": n_params, "ms_per_step": ms_per_step, "pass1_ms": statistics.mean(p1),
+        "pass2_ms": p2_ms, "bytes_per_param": p1b + p2b, "pass2_bytes_per_param": p2b,
+        "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<pass2>",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": (None if traffic_pp is None else int(traffic_pp * n_params))},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": 2 * K,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="luma", choices=["luma", "reference"])
+    ap.add_argument("--config", default="llama8b", choices=sorted(CONFIGS))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = CONFIGS[args.config]
+    p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
+    dtype = "f32 math; params " + str(cfg["pdt"]).replace("torch.", "") + ", grads " + \
+        str(cfg["gdt"]).replace("torch.", "") + ", codes int16"
+    config_out = {"workload": cfg["name"], "bytes_per_param": p1b + p2b,
+                  "l2": "inputs larger than L2 (resident params+grads+codes >> 126 MB)"
+                  if args.config in ("llama8b", "ragged") else "working set may fit L2",
+                  "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(args.config, args.steps, args.warmup, budget_s=60.0)
+        line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "Gparams/s",
+                "n_gpus": args.gpus, "steps": cb["steps_timed"], "warmup": max(args.warmup, 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": dtype, "data": "synthetic", "config": config_out,
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "Gparams/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    res = run_luma(args, rank, world, local_rank)
+    if rank == 0:
+        n = res["n_params"] * world
+        ms = res["ms_per_step"]
+        value = n / (ms * 1e-3) / 1e9
+        hbm = res["n_params"] * res["bytes_per_param"] / (ms * 1e-3) / 1e9
+        peak, peak_kind = measured_peak()
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "Gparams/s",
+                "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 1),
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config_out,
+                "hbm_gbs_per_gpu": round(hbm, 1),
+                "hbm_frac_of_measured_peak": round(hbm / peak, 4),
+                "hbm_frac_of_nominal_8tbs": round(hbm / NOMINAL_HBM_GBS, 4),
+                "pass1_ms": round(res["pass1_ms"], 4), "pass2_ms": round(res["pass2_ms"], 4),
+                "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
+                "gpu_launches": res["gpu_launches"]}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.config, 10, 2)
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,202 @@
+/*
+ * luma_b200.h — C ABI of the B200 (sm_100a) LUMA optimizer step.
+ *
+ * LUMA keeps AdamW's two moments as int16 codes on a per-tensor logarithmic
+ * grid (Q_m: signed momentum codes, Q_w: unsigned preconditioner codes stored
+ * in int16 bits) with per-tensor scales S_m = max|m|, S_v = max v.  One step
+ * decodes the codes, forms the new EMAs, applies the decoupled-weight-decay
+ * AdamW update, finds the new scales and re-quantizes onto the grid those
+ * scales define, with unbiased log-to-linear stochastic rounding (LogSR).
+ *
+ * This library runs that step for many tensors at once as two kernel
+ * launches over a device-resident descriptor table:
+ *   pass 1: decode -> EMA -> per-tensor max|m'|, max v'  (the last CTA to
+ *           finish a tensor turns the maxima into the next log grid);
+ *   pass 2: decode -> EMA -> AdamW update of the param (fp32 or bf16, in
+ *           place) -> LogSR re-quantization of m', v' (int16, in place).
+ *
+ * Every entry point is plain C: raw device pointers, sizes and a CUDA stream
+ * handle (cudaStream_t passed as void*).  Nothing here allocates device
+ * memory; the caller owns every buffer.  Calls are asynchronous on `stream`
+ * and return a status code (LUMA_OK on success; luma_last_error() gives the
+ * message of the last failure on the calling thread).
+ *
+ * Reference interfaces replaced (IgorYashch/LUMA, src/luma_optimizer/):
+ *   luma_step  <- triton_kernel.py:449-492  luma_triton_step(...)
+ *                 triton_kernel.py:409-446  luma_triton_init_step(...)
+ *                 functional.py:231-298     luma_update_step(...)
+ *                 functional.py:183-228     luma_init_step(...)
+ *              (one call steps every tensor whose descriptor is in the
+ *               table; the reference calls one of those per tensor from the
+ *               per-parameter loop at optimizer.py:422-522)
+ *   LumaGrid   <- functional.py:74-92 _precompute(S_m, S_v, eps) outputs,
+ *                 triton_kernel.py:34-36 new_grid[8] buffer layout
+ *   LumaStepRow<- functional.py:262-264 host scalars (bc1, bc2, eta_t) and
+ *                 optimizer.py:423-426 per-group hyper-parameters
+ */
+#ifndef LUMA_B200_H
+#define LUMA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LUMA_ABI_VERSION 1
+
+/* Quantization grid constants (reference config.py:23-25). */
+#define LUMA_K_M 32767        /* signed int16 magnitude of Q_m        */
+#define LUMA_K_W 65535        /* unsigned 16-bit range of Q_w         */
+#define LUMA_SCALE_FLOOR_M 1e-9
+
+/* Element types of params and grads. */
+enum {
+  LUMA_F32 = 0,
+  LUMA_BF16 = 1,
+  LUMA_F16 = 2
+};
+
+/* Status codes. */
+enum {
+  LUMA_OK = 0,
+  LUMA_ERR_INVALID = 1,     /* bad argument: null pointer, bad dtype, size */
+  LUMA_ERR_CUDA = 2,        /* a CUDA runtime call failed                 */
+  LUMA_ERR_UNSUPPORTED = 3  /* current device is not sm_100               */
+};
+
+/*
+ * One tensor (or one shard segment of a tensor) to step.  Device pointers.
+ * The table handed to luma_step must be sorted by oct_begin, with
+ * oct_begin[i+1] == oct_begin[i] + ceil(numel[i] / 8): the flat work space is
+ * counted in octets (groups of 8 elements) so every split point is 8-aligned.
+ */
+typedef struct LumaTensorDesc {
+  void*        param;        /* fp32 or bf16 [numel], updated in place      */
+  const void*  grad;         /* fp32, bf16 or fp16 [numel]                  */
+  int16_t*     q_m;          /* int16 [numel] momentum codes, in place      */
+  int16_t*     q_w;          /* int16 [numel] preconditioner codes (uint16
+                                bits), in place                             */
+  const float* u_m;          /* test hook: injected uniforms for Q_m, or NULL
+                                for the Philox4x32-10 stream                */
+  const float* u_w;          /* test hook: injected uniforms for Q_w, or NULL */
+  int64_t      numel;        /* elements (>= 1)                             */
+  int64_t      oct_begin;    /* first octet of this tensor in the flat space */
+  int64_t      rng_offset;   /* Philox counter of element 0 (multiple of 8);
+                                a shard segment passes its offset inside the
+                                full tensor                                 */
+  int32_t      param_id;     /* reference parameter index (seed mixing)     */
+  int32_t      row;          /* index into the LumaStepRow table            */
+  int32_t      slot;         /* index into the LumaSlot state array         */
+  uint8_t      param_dtype;  /* LUMA_F32 | LUMA_BF16                        */
+  uint8_t      grad_dtype;   /* LUMA_F32 | LUMA_BF16 | LUMA_F16             */
+  uint8_t      vec_ok;       /* 1 if param/grad/q_m/q_w/u_m/u_w are 16-byte
+                                aligned (128-bit vector path)               */
+  uint8_t      reserved0;
+  int64_t      reserved1;
+} LumaTensorDesc;            /* 96 bytes */
+
+/*
+ * Per-step scalars of one (param group, step) class, computed on the host in
+ * float64 exactly as the reference does and rounded to float32 where the
+ * reference's tensor ops round a Python scalar (functional.py:259-279).
+ */
+typedef struct LumaStepRow {
+  int64_t step;      /* t after the increment (optimizer.py:457); 1 = first step */
+  double  eps;       /* group eps, float64 (grid precompute)                */
+  float   beta1;     /* fl32(beta1)                                          */
+  float   omb1;      /* fl32(1 - beta1)                                      */
+  float   beta2;     /* fl32(beta2)                                          */
+  float   omb2;      /* fl32(1 - beta2)                                      */
+  float   decay;     /* fl32(1 - weight_decay * lr)                          */
+  float   neg_eta;   /* fl32(-(lr / (1 - beta1^t)))                          */
+  float   inv_bc2;   /* fl32(1 / fl32(1 - beta2^t)): tensor / scalar on CUDA */
+  float   eps32;     /* fl32(eps)                                            */
+  float   w_max;     /* fl32(1 / eps)                                        */
+  float   reserved;
+} LumaStepRow;       /* 56 bytes */
+
+/*
+ * One log grid (functional.py:74-92 evaluated for (S_m, S_v, eps)), with the
+ * float32 values the element-wise code consumes.
+ */
+typedef struct LumaGrid {
+  double  S_m;       /* max(max|m|, 1e-9), as the reference stores it       */
+  double  S_v;       /* max(max v, 0)                                        */
+  double  eps;       /* eps the float32 fields below were derived with      */
+  float   dm;        /* fl32(delta_m)                                        */
+  float   inv_dm;    /* fl32(1 / fl32(delta_m))                              */
+  float   inv_zm;    /* fl32(1 / fl32(z_m))                                  */
+  float   s_m32;     /* fl32(S_m) (momentum clamp)                           */
+  float   w_min;     /* fl32(w_min)                                          */
+  float   inv_wmin;  /* fl32(1 / fl32(w_min))                                */
+  float   dw;        /* fl32(delta_w)                                        */
+  float   inv_dw;    /* fl32(1 / fl32(delta_w)), 0 when delta_w == 0         */
+  float   inv_zw;    /* fl32(1 / fl32(z_w))                                  */
+  int32_t dw_pos;    /* delta_w > 0                                          */
+} LumaGrid;          /* 64 bytes */
+
+/*
+ * Device state of one descriptor.  grid[t & 1] holds the grid the codes were
+ * written on at step t; step t decodes with grid[(t - 1) & 1] and encodes
+ * with grid[t & 1].  amax_m/amax_v/done are pass-1 accumulators: zero before
+ * a step, reset to zero by the CTA that finishes the tensor.  A new slot must
+ * be zero-filled.
+ */
+typedef struct LumaSlot {
+  LumaGrid grid[2];
+  uint32_t amax_m;   /* bits of max |m'| (non-negative float order)         */
+  uint32_t amax_v;   /* bits of max v'                                       */
+  uint64_t done;     /* octets of this tensor finished by pass 1            */
+} LumaSlot;          /* 144 bytes */
+
+typedef struct LumaStepArgs {
+  const LumaTensorDesc* descs;    /* device [n_desc], sorted by oct_begin   */
+  LumaSlot*             slots;    /* device state array                     */
+  const LumaStepRow*    rows;     /* device [n_rows]                        */
+  int32_t               n_desc;
+  int32_t               n_rows;
+  int64_t               total_octets; /* oct_begin[last] + octets(last)     */
+  int64_t               base_seed;    /* optimizer._base_seed (optimizer.py:94-96) */
+  void*                 events[3];    /* optional cudaEvent_t recorded before
+                                         pass 1, between the passes and after
+                                         pass 2 (timing); NULL to skip      */
+} LumaStepArgs;
+
+/*
+ * Run one LUMA step for every descriptor: two launches on `stream`, no host
+ * synchronisation, no allocation.  Descriptors whose row has step == 1 take
+ * the reference's first-step path (zero-initialised moments, functional.py:
+ * 183-228); the others decode their codes (functional.py:231-298).
+ */
+int luma_step(const LumaStepArgs* args, void* stream);
+
+/*
+ * Decode codes to float32 AdamW moments (reference optimizer.py:231-235 /
+ * functional.py:113-126): exp_avg[i] = sign(q_m) expm1(|q_m| dm),
+ * w = w_min exp(q_w dw), exp_avg_sq[i] = max(1/w - eps32, 0)^2, with the
+ * float32 grid values dm = fl32(delta_m), w_min = fl32(w_min),
+ * dw = fl32(delta_w) of _precompute(S_m, S_v, eps) and eps32 = fl32(eps).
+ */
+int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel,
+                float dm, float w_min, float dw, float eps32,
+                float* exp_avg, float* exp_avg_sq, void* stream);
+
+/* ABI version (LUMA_ABI_VERSION). */
+int luma_abi_version(void);
+
+/*
+ * Layout check for FFI callers: writes sizeof of LumaTensorDesc, LumaStepRow,
+ * LumaGrid, LumaSlot, LumaStepArgs into out[0..4] and returns 5 (or fewer if
+ * n < 5).
+ */
+int luma_struct_sizes(int64_t* out, int n);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* luma_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUMA_B200_H */

@@ -1,0 +1,131 @@
+"""ctypes binding of ``libluma_b200.so`` (the C ABI in include/luma_b200.h).
+
+The shared library is built in-tree (``luma_b200/_lib/libluma_b200.so``, see
+``luma_b200/build.py``).  There is no fallback: if the library is missing or
+its struct layout disagrees with the numpy mirrors below, ``lib()`` raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import numpy as np
+
+LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
+LIB_PATH = os.path.join(LIB_DIR, "libluma_b200.so")
+
+ABI_VERSION = 1
+
+LUMA_OK = 0
+LUMA_ERR_INVALID = 1
+LUMA_ERR_CUDA = 2
+LUMA_ERR_UNSUPPORTED = 3
+
+F32, BF16, F16 = 0, 1, 2
+
+# numpy mirrors of the C structs (include/luma_b200.h); offsets are explicit
+# so a layout drift fails the size check in lib().
+DESC_DTYPE = np.dtype({
+    "names": ["param", "grad", "q_m", "q_w", "u_m", "u_w", "numel", "oct_begin", "rng_offset",
+              "param_id", "row", "slot", "param_dtype", "grad_dtype", "vec_ok", "reserved0",
+              "reserved1"],
+    "formats": ["<u8", "<u8", "<u8", "<u8", "<u8", "<u8", "<i8", "<i8", "<i8",
+                "<i4", "<i4", "<i4", "u1", "u1", "u1", "u1", "<i8"],
+    "offsets": [0, 8, 16, 24, 32, 40, 48, 56, 64, 72, 76, 80, 84, 85, 86, 87, 88],
+    "itemsize": 96,
+})
+
+ROW_DTYPE = np.dtype({
+    "names": ["step", "eps", "beta1", "omb1", "beta2", "omb2", "decay", "neg_eta", "inv_bc2",
+              "eps32", "w_max", "reserved"],
+    "formats": ["<i8", "<f8"] + ["<f4"] * 10,
+    "offsets": [0, 8, 16, 20, 24, 28, 32, 36, 40, 44, 48, 52],
+    "itemsize": 56,
+})
+
+GRID_DTYPE = np.dtype({
+    "names": ["S_m", "S_v", "eps", "dm", "inv_dm", "inv_zm", "s_m32", "w_min", "inv_wmin", "dw",
+              "inv_dw", "inv_zw", "dw_pos"],
+    "formats": ["<f8", "<f8", "<f8"] + ["<f4"] * 9 + ["<i4"],
+    "offsets": [0, 8, 16, 24, 28, 32, 36, 40, 44, 48, 52, 56, 60],
+    "itemsize": 64,
+})
+
+SLOT_DTYPE = np.dtype({
+    "names": ["grid", "amax_m", "amax_v", "done"],
+    "formats": [(GRID_DTYPE, (2,)), "<u4", "<u4", "<u8"],
+    "offsets": [0, 128, 132, 136],
+    "itemsize": 144,
+})
+
+
+class LumaStepArgs(ctypes.Structure):
+    _fields_ = [
+        ("descs", ctypes.c_void_p),
+        ("slots", ctypes.c_void_p),
+        ("rows", ctypes.c_void_p),
+        ("n_desc", ctypes.c_int32),
+        ("n_rows", ctypes.c_int32),
+        ("total_octets", ctypes.c_int64),
+        ("base_seed", ctypes.c_int64),
+        ("events", ctypes.c_void_p * 3),
+    ]
+
+
+EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
+                  SLOT_DTYPE.itemsize, ctypes.sizeof(LumaStepArgs))
+
+EXPORTED = ("luma_step", "luma_decode", "luma_abi_version", "luma_struct_sizes",
+            "luma_last_error")
+
+_lib = None
+_lock = threading.Lock()
+
+
+class LumaError(RuntimeError):
+    """A call into libluma_b200 returned an error status."""
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the shared library, checking ABI and layout."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"libluma_b200.so not found at {LIB_PATH}; build it with "
+                f"`python -m luma_b200.build` (nvcc, sm_100a)")
+        h = ctypes.CDLL(LIB_PATH)
+        h.luma_abi_version.restype = ctypes.c_int
+        h.luma_abi_version.argtypes = []
+        h.luma_struct_sizes.restype = ctypes.c_int
+        h.luma_struct_sizes.argtypes = [ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
+        h.luma_last_error.restype = ctypes.c_char_p
+        h.luma_last_error.argtypes = []
+        h.luma_step.restype = ctypes.c_int
+        h.luma_step.argtypes = [ctypes.POINTER(LumaStepArgs), ctypes.c_void_p]
+        h.luma_decode.restype = ctypes.c_int
+        h.luma_decode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                  ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        v = h.luma_abi_version()
+        if v != ABI_VERSION:
+            raise ImportError(f"libluma_b200 ABI {v}, expected {ABI_VERSION}")
+        sizes = (ctypes.c_int64 * 5)()
+        h.luma_struct_sizes(sizes, 5)
+        if tuple(sizes) != EXPECTED_SIZES:
+            raise ImportError(f"libluma_b200 struct sizes {tuple(sizes)} != {EXPECTED_SIZES}")
+        _lib = h
+        return h
+
+
+def check(status: int, what: str) -> None:
+    if status != LUMA_OK:
+        msg = lib().luma_last_error().decode(errors="replace")
+        kind = {LUMA_ERR_INVALID: ValueError, LUMA_ERR_UNSUPPORTED: RuntimeError}.get(status, LumaError)
+        raise kind(f"{what} failed (status {status}): {msg}")

@@ -1,0 +1,678 @@
+// luma_step.cu — sm_100a kernels and C ABI of the LUMA optimizer step.
+//
+// The step is the reference's two-pass matched-scaling update
+// (IgorYashch/LUMA src/luma_optimizer/functional.py:183-298), run for every
+// tensor of the optimizer in two launches over a device descriptor table:
+//
+//   pass 1  decode (Q_m, Q_w) on the tensor's current grid -> EMA with the
+//           gradient -> per-thread max |m'|, max v' -> warp/block reduction ->
+//           one atomicMax per (CTA, tensor) on the float bit patterns (order-
+//           independent, so deterministic).  The CTA whose octet count closes
+//           the tensor (atomic counter, no spinning) turns the two maxima into
+//           the next grid in float64 (functional.py:74-92, 282-292).
+//   pass 2  decode -> EMA (recomputed: no temporaries) -> AdamW update of the
+//           param in place -> LogSR re-quantization on the new grid with
+//           Philox4x32-10 uniforms (or injected uniforms, the test hook).
+//
+// Arithmetic follows the reference op by op as PyTorch's CUDA kernels execute
+// it (each op rounds to float32 on its own; a tensor divided by a Python
+// scalar is a multiply by the float32 reciprocal; addcdiv is one fma), so the
+// codes and params are bit-identical to the reference running on CUDA when
+// both consume the same uniforms.  No fast-math: expm1f, expf, log1pf, logf,
+// IEEE division and sqrt are the CUDA library's accurate versions, the same
+// functions PyTorch's element-wise kernels call.
+//
+// Work split: the flat space of all tensors, counted in octets (8 elements),
+// is cut into one contiguous range per CTA of a persistent grid sized from the
+// occupancy calculator.  A CTA walks the tensors its range overlaps; each
+// thread owns one octet per iteration (128-bit loads/stores when aligned).
+
+#include "luma_b200.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+static_assert(sizeof(LumaTensorDesc) == 96, "LumaTensorDesc layout");
+static_assert(sizeof(LumaStepRow) == 56, "LumaStepRow layout");
+static_assert(sizeof(LumaGrid) == 64, "LumaGrid layout");
+static_assert(sizeof(LumaSlot) == 144, "LumaSlot layout");
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// ---------------------------------------------------------------------------
+// Error reporting
+// ---------------------------------------------------------------------------
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(LUMA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------------------
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel Random Numbers: As Easy
+// as 1, 2, 3", SC'11): 10 rounds of two 32x32->64 multiplies with the key
+// bumped by the Weyl constants between rounds.
+// ---------------------------------------------------------------------------
+
+constexpr uint32_t kPhiloxM0 = 0xD2511F53u;
+constexpr uint32_t kPhiloxM1 = 0xCD9E8D57u;
+constexpr uint32_t kPhiloxW0 = 0x9E3779B9u;
+constexpr uint32_t kPhiloxW1 = 0xBB67AE85u;
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = kPhiloxM0 * c.x;
+    const uint32_t hi0 = __umulhi(kPhiloxM0, c.x);
+    const uint32_t lo1 = kPhiloxM1 * c.z;
+    const uint32_t hi1 = __umulhi(kPhiloxM1, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += kPhiloxW0;
+    k1 += kPhiloxW1;
+  }
+  return c;
+}
+
+// Top 24 bits of a Philox word as a float32 uniform in [0, 1) (exact).
+__device__ __forceinline__ float u24(uint32_t x) {
+  return __uint2float_rn(x >> 8) * 0x1.0p-24f;
+}
+
+// ---------------------------------------------------------------------------
+// Grid precompute, float64 on device (reference functional.py:74-92).
+// ---------------------------------------------------------------------------
+
+__device__ void make_grid(double S_m, double S_v, double eps, LumaGrid* g) {
+  const double w_min = 1.0 / (sqrt(S_v) + eps);
+  const double delta_m = log1p(S_m) / (double)LUMA_K_M;
+  const double z_m = expm1(delta_m);
+  const double ratio = 1.0 / (eps * w_min);
+  const double delta_w = (ratio > 1.0) ? log(ratio) / (double)LUMA_K_W : 0.0;
+  const double z_w = (delta_w > 0.0) ? expm1(delta_w) : 1.0;
+  g->S_m = S_m;
+  g->S_v = S_v;
+  g->eps = eps;
+  const float dm = __double2float_rn(delta_m);
+  g->dm = dm;
+  g->inv_dm = __fdiv_rn(1.0f, dm);
+  g->inv_zm = __fdiv_rn(1.0f, __double2float_rn(z_m));
+  g->s_m32 = __double2float_rn(S_m);
+  const float wmin = __double2float_rn(w_min);
+  g->w_min = wmin;
+  g->inv_wmin = __fdiv_rn(1.0f, wmin);
+  const float dw = __double2float_rn(delta_w);
+  g->dw = dw;
+  g->inv_dw = (delta_w > 0.0) ? __fdiv_rn(1.0f, dw) : 0.0f;
+  g->inv_zw = __fdiv_rn(1.0f, __double2float_rn(z_w));
+  g->dw_pos = (delta_w > 0.0) ? 1 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// Element arithmetic.  Every helper names the reference expression it
+// evaluates; each torch op of the reference is one correctly rounded fp32 op.
+// ---------------------------------------------------------------------------
+
+// torch.clamp_min / clamp keep NaN (ATen clamp kernels return NaN inputs).
+__device__ __forceinline__ float clamp_min_keepnan(float x, float lo) {
+  return isnan(x) ? x : fmaxf(x, lo);
+}
+__device__ __forceinline__ float clamp_keepnan(float x, float lo, float hi) {
+  return isnan(x) ? x : fminf(fmaxf(x, lo), hi);
+}
+
+struct Consts {
+  // step row
+  float beta1, omb1, beta2, omb2, decay, neg_eta, inv_bc2, eps32, w_max;
+  // decode grid (codes as stored)
+  float o_dm, o_wmin, o_dw;
+  // encode grid (this step's new scales), pass 2 only
+  float n_sm32, n_dm, n_inv_dm, n_inv_zm, n_wmin, n_inv_wmin, n_dw, n_inv_dw, n_inv_zw;
+  int n_dw_pos;
+  int init;
+};
+
+// m = sgn(Q_m) * expm1(|Q_m| * delta_m)       functional.py:113-116
+__device__ __forceinline__ float decode_m(int q, float dm) {
+  const float e = expm1f(__fmul_rn((float)abs(q), dm));
+  return q < 0 ? -e : e;
+}
+
+// w = w_min * exp(Q_w * delta_w)               functional.py:119-126
+// v = (1.0 / w - eps).clamp_min(0).square()    functional.py:270
+__device__ __forceinline__ float decode_v(uint32_t qu, float wmin, float dw, float eps32) {
+  const float w = __fmul_rn(wmin, expf(__fmul_rn((float)qu, dw)));
+  const float t = clamp_min_keepnan(__fsub_rn(__fdiv_rn(1.0f, w), eps32), 0.0f);
+  return __fmul_rn(t, t);
+}
+
+// m' = beta1 * m + (1 - beta1) * g ;  v' = beta2 * v + (1 - beta2) * g^2
+// (functional.py:274-275; first step functional.py:204-205 with m = v = 0).
+__device__ __forceinline__ void ema(const Consts& c, float g, float m, float v,
+                                    float& mn, float& vn) {
+  const float g2 = __fmul_rn(g, g);
+  if (c.init) {
+    mn = __fmul_rn(c.omb1, g);
+    vn = __fmul_rn(c.omb2, g2);
+  } else {
+    mn = __fadd_rn(__fmul_rn(c.beta1, m), __fmul_rn(c.omb1, g));
+    vn = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, g2));
+  }
+}
+
+// param.mul_(1 - wd*lr); param.addcdiv_(m', sqrt(v'/bc2) + eps, value=-eta)
+// (functional.py:278-279, 213-214).  v'/bc2 is v' * fl32(1/fl32(bc2)) on
+// CUDA; addcdiv is fma(value, m'/den, param).
+__device__ __forceinline__ float adamw(const Consts& c, float p, float mn, float vn) {
+  const float pd = __fmul_rn(p, c.decay);
+  const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vn, c.inv_bc2)), c.eps32);
+  return __fmaf_rn(c.neg_eta, __fdiv_rn(mn, den), pd);
+}
+
+// _quantize_momentum (functional.py:133-150) with _log_sr (functional.py:38-67).
+__device__ __forceinline__ int quant_m(const Consts& c, float mn, float u) {
+  const float mc = clamp_keepnan(mn, -c.n_sm32, c.n_sm32);
+  const float y = __fmul_rn(log1pf(fabsf(mc)), c.n_inv_dm);
+  const float fy = floorf(y);
+  const float fr = __fsub_rn(y, fy);
+  const float ps = __fmul_rn(expm1f(__fmul_rn(fr, c.n_dm)), c.n_inv_zm);
+  float r = __fadd_rn(fy, (u < ps) ? 1.0f : 0.0f);
+  r = clamp_keepnan(r, 0.0f, (float)LUMA_K_M);
+  const float sg = (mc > 0.0f) ? 1.0f : ((mc < 0.0f) ? -1.0f : 0.0f);
+  return (int)__fmul_rn(sg, r);
+}
+
+// _quantize_preconditioner (functional.py:153-176) with _log_sr.
+__device__ __forceinline__ uint32_t quant_w(const Consts& c, float vn, float u) {
+  if (!c.n_dw_pos) return 0u;  // delta_w == 0: y = 0 and _log_sr returns 0
+  const float den = __fadd_rn(__fsqrt_rn(clamp_min_keepnan(vn, 0.0f)), c.eps32);
+  const float w = clamp_keepnan(__fdiv_rn(1.0f, den), c.n_wmin, c.w_max);
+  const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
+  const float fy = floorf(y);
+  const float fr = __fsub_rn(y, fy);
+  const float ps = __fmul_rn(expm1f(__fmul_rn(fr, c.n_dw)), c.n_inv_zw);
+  float r = __fadd_rn(fy, (u < ps) ? 1.0f : 0.0f);
+  r = clamp_keepnan(r, 0.0f, (float)LUMA_K_W);
+  return (uint32_t)(int)r;  // .to(int32) then two's-complement wrap to int16
+}
+
+// ---------------------------------------------------------------------------
+// Octet loads and stores
+// ---------------------------------------------------------------------------
+
+template <int DT>
+__device__ __forceinline__ void load8(const void* base, int64_t e0, int n, bool vec, float (&x)[8]) {
+  if (DT == LUMA_F32) {
+    const float* p = static_cast<const float*>(base) + e0;
+    if (vec) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(p));
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+      x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] = (j < n) ? p[j] : 0.0f;
+    }
+  } else {
+    const uint16_t* p = static_cast<const uint16_t*>(base) + e0;
+    uint16_t h[8];
+    if (vec) {
+      const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
+      memcpy(h, &a, 16);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = (j < n) ? p[j] : (uint16_t)0;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (DT == LUMA_BF16) {
+        x[j] = __uint_as_float((uint32_t)h[j] << 16);  // bf16 -> f32 is exact
+      } else {
+        x[j] = __half2float(__ushort_as_half(h[j]));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void load8_codes(const int16_t* base, int64_t e0, int n, bool vec,
+                                            uint16_t (&q)[8]) {
+  const uint16_t* p = reinterpret_cast<const uint16_t*>(base) + e0;
+  if (vec) {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(p));
+    memcpy(q, &a, 16);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = (j < n) ? p[j] : (uint16_t)0;
+  }
+}
+
+__device__ __forceinline__ void load8_f32_plain(const float* base, int64_t e0, int n, bool vec,
+                                                float (&x)[8]) {
+  load8<LUMA_F32>(base, e0, n, vec, x);
+}
+
+template <int DT>
+__device__ __forceinline__ void store8(void* base, int64_t e0, int n, bool vec, const float (&x)[8]) {
+  if (DT == LUMA_F32) {
+    float* p = static_cast<float*>(base) + e0;
+    if (vec) {
+      __stcs(reinterpret_cast<float4*>(p), make_float4(x[0], x[1], x[2], x[3]));
+      __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(x[4], x[5], x[6], x[7]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) p[j] = x[j];
+    }
+  } else {  // bf16, round to nearest even
+    uint16_t* p = static_cast<uint16_t*>(base) + e0;
+    uint16_t h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = __bfloat16_as_ushort(__float2bfloat16_rn(x[j]));
+    if (vec) {
+      uint4 a;
+      memcpy(&a, h, 16);
+      __stcs(reinterpret_cast<uint4*>(p), a);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) p[j] = h[j];
+    }
+  }
+}
+
+__device__ __forceinline__ void store8_codes(int16_t* base, int64_t e0, int n, bool vec,
+                                             const uint16_t (&q)[8]) {
+  uint16_t* p = reinterpret_cast<uint16_t*>(base) + e0;
+  if (vec) {
+    uint4 a;
+    memcpy(&a, q, 16);
+    __stcs(reinterpret_cast<uint4*>(p), a);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < n) p[j] = q[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-tensor segment bodies
+// ---------------------------------------------------------------------------
+
+// Pass 1 body: returns this thread's max |m'| and max v' bit patterns.
+template <int GD>
+__device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Consts& c,
+                                             int64_t o_lo, int64_t o_hi,
+                                             uint32_t& am, uint32_t& av) {
+  for (int64_t o = o_lo + threadIdx.x; o < o_hi; o += kThreads) {
+    const int64_t e0 = o * 8;
+    const int64_t rem = d.numel - e0;
+    const int n = rem < 8 ? (int)rem : 8;
+    const bool vec = d.vec_ok != 0 && n == 8;  // 128-bit path only for full octets
+    float g[8];
+    load8<GD>(d.grad, e0, n, vec, g);
+    uint16_t qm[8], qw[8];
+    if (!c.init) {
+      load8_codes(d.q_m, e0, n, vec, qm);
+      load8_codes(d.q_w, e0, n, vec, qw);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < n) {
+        float m = 0.0f, v = 0.0f;
+        if (!c.init) {
+          m = decode_m((int)(int16_t)qm[j], c.o_dm);
+          v = decode_v((uint32_t)qw[j], c.o_wmin, c.o_dw, c.eps32);
+        }
+        float mn, vn;
+        ema(c, g[j], m, v, mn, vn);
+        am = max(am, __float_as_uint(fabsf(mn)));
+        av = max(av, __float_as_uint(vn));
+      }
+    }
+  }
+}
+
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_octets(const LumaTensorDesc& d, const Consts& c,
+                                             uint32_t k0, uint32_t k1,
+                                             int64_t o_lo, int64_t o_hi) {
+  const bool injected = d.u_m != nullptr;
+  for (int64_t o = o_lo + threadIdx.x; o < o_hi; o += kThreads) {
+    const int64_t e0 = o * 8;
+    const int64_t rem = d.numel - e0;
+    const int n = rem < 8 ? (int)rem : 8;
+    const bool vec = d.vec_ok != 0 && n == 8;  // 128-bit path only for full octets
+    float p[8], g[8];
+    load8<PD>(d.param, e0, n, vec, p);
+    load8<GD>(d.grad, e0, n, vec, g);
+    uint16_t qm[8], qw[8];
+    if (!c.init) {
+      load8_codes(d.q_m, e0, n, vec, qm);
+      load8_codes(d.q_w, e0, n, vec, qw);
+    }
+    float um[8], uw[8];
+    if (injected) {
+      load8_f32_plain(d.u_m, e0, n, vec, um);
+      load8_f32_plain(d.u_w, e0, n, vec, uw);
+    } else {
+      // element e draws Philox block ((rng_offset + e) / 2): words 0,1 for the
+      // even element of the pair, words 2,3 for the odd one (u_m, u_w).
+      const uint64_t pair0 = (uint64_t)(d.rng_offset + e0) >> 1;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint64_t ctr = pair0 + k;
+        const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+        um[2 * k] = u24(r.x);
+        uw[2 * k] = u24(r.y);
+        um[2 * k + 1] = u24(r.z);
+        uw[2 * k + 1] = u24(r.w);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float m = 0.0f, v = 0.0f;
+      if (!c.init) {
+        m = decode_m((int)(int16_t)qm[j], c.o_dm);
+        v = decode_v((uint32_t)qw[j], c.o_wmin, c.o_dw, c.eps32);
+      }
+      float mn, vn;
+      ema(c, g[j], m, v, mn, vn);
+      p[j] = adamw(c, p[j], mn, vn);
+      qm[j] = (uint16_t)(int16_t)quant_m(c, mn, um[j]);
+      qw[j] = (uint16_t)quant_w(c, vn, uw[j]);
+    }
+    store8<PD>(d.param, e0, n, vec, p);
+    store8_codes(d.q_m, e0, n, vec, qm);
+    store8_codes(d.q_w, e0, n, vec, qw);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernels
+// ---------------------------------------------------------------------------
+
+struct SegShared {
+  LumaTensorDesc d;
+  LumaStepRow row;
+  LumaGrid dec;
+  LumaGrid enc;
+  int64_t next_pos;
+};
+
+// Largest i with descs[i].oct_begin <= pos.
+__device__ int find_desc(const LumaTensorDesc* descs, int n, int64_t pos) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (descs[mid].oct_begin <= pos) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Consts& c) {
+  c.beta1 = s.row.beta1; c.omb1 = s.row.omb1; c.beta2 = s.row.beta2; c.omb2 = s.row.omb2;
+  c.decay = s.row.decay; c.neg_eta = s.row.neg_eta; c.inv_bc2 = s.row.inv_bc2;
+  c.eps32 = s.row.eps32; c.w_max = s.row.w_max;
+  c.init = (s.row.step == 1) ? 1 : 0;
+  c.o_dm = s.dec.dm; c.o_wmin = s.dec.w_min; c.o_dw = s.dec.dw;
+  if (pass2) {
+    c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
+    c.n_wmin = s.enc.w_min; c.n_inv_wmin = s.enc.inv_wmin; c.n_dw = s.enc.dw;
+    c.n_inv_dw = s.enc.inv_dw; c.n_inv_zw = s.enc.inv_zw; c.n_dw_pos = s.enc.dw_pos;
+  }
+}
+
+// Thread 0: load descriptor `di`, its row and grids into shared memory.
+__device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShared& s) {
+  s.d = a.descs[di];
+  s.row = a.rows[s.d.row];
+  const LumaSlot* slot = a.slots + s.d.slot;
+  const int64_t t = s.row.step;
+  if (t != 1) {
+    s.dec = slot->grid[(t - 1) & 1];
+    // The stored grid was derived with the eps of its own step; the reference
+    // re-derives the decode grid from (S_m, S_v) with the current eps.
+    if (s.dec.eps != s.row.eps) make_grid(s.dec.S_m, s.dec.S_v, s.row.eps, &s.dec);
+  }
+  if (pass2) s.enc = slot->grid[t & 1];
+}
+
+template <bool PASS2>
+__global__ void __launch_bounds__(kThreads) luma_pass_kernel(const LumaStepArgs a) {
+  __shared__ SegShared s;
+  __shared__ uint32_t red_m[kWarps], red_v[kWarps];
+  __shared__ int s_di;
+
+  const int64_t T = a.total_octets;
+  const int64_t lo = (T * (int64_t)blockIdx.x) / (int64_t)gridDim.x;
+  const int64_t hi = (T * ((int64_t)blockIdx.x + 1)) / (int64_t)gridDim.x;
+  if (lo >= hi) return;
+
+  if (threadIdx.x == 0) s_di = find_desc(a.descs, a.n_desc, lo);
+  __syncthreads();
+  int di = s_di;
+  int64_t pos = lo;
+  while (pos < hi && di < a.n_desc) {
+    if (threadIdx.x == 0) load_segment(a, di, PASS2, s);
+    __syncthreads();
+    const LumaTensorDesc& d = s.d;
+    const int64_t n_oct = (d.numel + 7) / 8;
+    const int64_t o_lo = pos - d.oct_begin;
+    const int64_t o_hi = min(hi - d.oct_begin, n_oct);
+    Consts c;
+    fill_consts(s, PASS2, c);
+
+    if (!PASS2) {
+      uint32_t am = 0u, av = 0u;
+      switch (d.grad_dtype) {
+        case LUMA_F32: pass1_octets<LUMA_F32>(d, c, o_lo, o_hi, am, av); break;
+        case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, o_lo, o_hi, am, av); break;
+        default: pass1_octets<LUMA_F16>(d, c, o_lo, o_hi, am, av); break;
+      }
+      am = __reduce_max_sync(0xffffffffu, am);
+      av = __reduce_max_sync(0xffffffffu, av);
+      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      if (lane == 0) { red_m[warp] = am; red_v[warp] = av; }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int w = 1; w < kWarps; ++w) { am = max(am, red_m[w]); av = max(av, red_v[w]); }
+        LumaSlot* slot = a.slots + d.slot;
+        atomicMax(&slot->amax_m, am);
+        atomicMax(&slot->amax_v, av);
+        __threadfence();
+        const unsigned long long mine = (unsigned long long)(o_hi - o_lo);
+        const unsigned long long prev = atomicAdd((unsigned long long*)&slot->done, mine);
+        if (prev + mine == (unsigned long long)n_oct) {
+          // Last contributor for this tensor: every other CTA's maxima are in.
+          __threadfence();
+          const uint32_t bm = atomicOr(&slot->amax_m, 0u);
+          const uint32_t bv = atomicOr(&slot->amax_v, 0u);
+          const double smt = (double)__uint_as_float(bm);
+          const double svt = (double)__uint_as_float(bv);
+          // S_m = max(S_m_t, 1e-9); S_v = max(S_v_t, 0.0) with Python's max()
+          // (first argument kept unless the second compares greater).
+          const double S_m = (LUMA_SCALE_FLOOR_M > smt) ? LUMA_SCALE_FLOOR_M : smt;
+          const double S_v = (0.0 > svt) ? 0.0 : svt;
+          make_grid(S_m, S_v, s.row.eps, &slot->grid[s.row.step & 1]);
+          slot->amax_m = 0u;
+          slot->amax_v = 0u;
+          slot->done = 0ull;
+        }
+      }
+    } else {
+      const uint64_t seed = ((uint64_t)s.row.step << 32 | (uint64_t)((int64_t)d.param_id * 2)) ^
+                            (uint64_t)a.base_seed;
+      const uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+      if (d.param_dtype == LUMA_F32) {
+        switch (d.grad_dtype) {
+          case LUMA_F32: pass2_octets<LUMA_F32, LUMA_F32>(d, c, k0, k1, o_lo, o_hi); break;
+          case LUMA_BF16: pass2_octets<LUMA_F32, LUMA_BF16>(d, c, k0, k1, o_lo, o_hi); break;
+          default: pass2_octets<LUMA_F32, LUMA_F16>(d, c, k0, k1, o_lo, o_hi); break;
+        }
+      } else {
+        switch (d.grad_dtype) {
+          case LUMA_F32: pass2_octets<LUMA_BF16, LUMA_F32>(d, c, k0, k1, o_lo, o_hi); break;
+          case LUMA_BF16: pass2_octets<LUMA_BF16, LUMA_BF16>(d, c, k0, k1, o_lo, o_hi); break;
+          default: pass2_octets<LUMA_BF16, LUMA_F16>(d, c, k0, k1, o_lo, o_hi); break;
+        }
+      }
+    }
+    __syncthreads();  // s is rewritten for the next tensor
+    pos = d.oct_begin + o_hi;
+    ++di;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) luma_decode_kernel(
+    const int16_t* __restrict__ q_m, const int16_t* __restrict__ q_w, int64_t n,
+    float dm, float wmin, float dw, float eps32, float* __restrict__ m_out,
+    float* __restrict__ v_out) {
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * kThreads) {
+    m_out[i] = decode_m((int)q_m[i], dm);
+    v_out[i] = decode_v((uint32_t)(uint16_t)q_w[i], wmin, dw, eps32);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+struct DeviceInfo {
+  bool ready = false;
+  int status = LUMA_OK;
+  int sms = 0;
+  int ctas_pass1 = 0;
+  int ctas_pass2 = 0;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(LUMA_ERR_INVALID, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& di = g_dev[dev];
+  if (!di.ready) {
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10) {
+      return fail(LUMA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                  dev, prop.major, prop.minor);
+    }
+    int b1 = 0, b2 = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, luma_pass_kernel<false>, kThreads, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass1)");
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, luma_pass_kernel<true>, kThreads, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass2)");
+    di.sms = prop.multiProcessorCount;
+    di.ctas_pass1 = di.sms * (b1 > 0 ? b1 : 1);
+    di.ctas_pass2 = di.sms * (b2 > 0 ? b2 : 1);
+    di.ready = true;
+  }
+  *out = &di;
+  return LUMA_OK;
+}
+
+int grid_for(int64_t total_octets, int max_ctas) {
+  // at least one full tile (kThreads octets) per CTA
+  const int64_t want = (total_octets + kThreads - 1) / kThreads;
+  return (int)(want < max_ctas ? (want > 0 ? want : 1) : max_ctas);
+}
+
+}  // namespace
+
+extern "C" {
+
+int luma_abi_version(void) { return LUMA_ABI_VERSION; }
+
+const char* luma_last_error(void) { return g_err; }
+
+int luma_struct_sizes(int64_t* out, int n) {
+  const int64_t sizes[5] = {(int64_t)sizeof(LumaTensorDesc), (int64_t)sizeof(LumaStepRow),
+                            (int64_t)sizeof(LumaGrid), (int64_t)sizeof(LumaSlot),
+                            (int64_t)sizeof(LumaStepArgs)};
+  if (out == nullptr || n <= 0) return 0;
+  const int k = n < 5 ? n : 5;
+  for (int i = 0; i < k; ++i) out[i] = sizes[i];
+  return k;
+}
+
+int luma_step(const LumaStepArgs* args, void* stream) {
+  g_err[0] = '\0';
+  if (args == nullptr) return fail(LUMA_ERR_INVALID, "luma_step: args is NULL");
+  const LumaStepArgs a = *args;
+  if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0)
+    return fail(LUMA_ERR_INVALID, "luma_step: negative size (n_desc=%d n_rows=%d total_octets=%lld)",
+                a.n_desc, a.n_rows, (long long)a.total_octets);
+  if (a.n_desc == 0 || a.total_octets == 0) return LUMA_OK;
+  if (a.descs == nullptr || a.slots == nullptr || a.rows == nullptr || a.n_rows == 0)
+    return fail(LUMA_ERR_INVALID, "luma_step: descs/slots/rows must be non-NULL and n_rows > 0");
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st != LUMA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (a.events[0]) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[0]), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  luma_pass_kernel<false><<<grid_for(a.total_octets, di->ctas_pass1), kThreads, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch pass 1");
+  if (a.events[1]) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[1]), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  luma_pass_kernel<true><<<grid_for(a.total_octets, di->ctas_pass2), kThreads, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
+  if (a.events[2]) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[2]), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  return LUMA_OK;
+}
+
+int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel, float dm, float w_min,
+                float dw, float eps32, float* exp_avg, float* exp_avg_sq, void* stream) {
+  g_err[0] = '\0';
+  if (numel < 0) return fail(LUMA_ERR_INVALID, "luma_decode: negative numel");
+  if (numel == 0) return LUMA_OK;
+  if (!q_m || !q_w || !exp_avg || !exp_avg_sq)
+    return fail(LUMA_ERR_INVALID, "luma_decode: NULL pointer");
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st != LUMA_OK) return st;
+  const int64_t blocks_needed = (numel + kThreads - 1) / kThreads;
+  const int blocks = (int)(blocks_needed < di->sms * 8 ? blocks_needed : di->sms * 8);
+  luma_decode_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      q_m, q_w, numel, dm, w_min, dw, eps32, exp_avg, exp_avg_sq);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch decode");
+  return LUMA_OK;
+}
+
+}  // extern "C"

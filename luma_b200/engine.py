@@ -1,0 +1,171 @@
+"""Device-side bookkeeping of the CUDA backend: descriptor table, state slots,
+per-step scalar rows, and the call into ``luma_step``.
+
+One ``DeviceEngine`` per CUDA device.  It owns three device buffers (all
+allocated through torch's caching allocator, never inside the step kernels):
+
+* ``descs``  — the LumaTensorDesc table.  Rebuilt only when a pointer, size,
+  row or slot of a segment changes (new grads, grads that went to None, a
+  checkpoint load), otherwise reused step after step;
+* ``slots``  — one LumaSlot per tensor (or shard segment): the two grids and
+  the pass-1 accumulators.  Zero-filled when created;
+* ``rows``   — the LumaStepRow table of this step, uploaded every step from
+  a small ring of pinned host buffers (an event guards each ring entry, so a
+  buffer is rewritten only after its copy has executed).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import DESC_DTYPE, GRID_DTYPE, ROW_DTYPE, SLOT_DTYPE
+
+_DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+_RING = 4
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    return _DTYPE_CODE[dt]
+
+
+@dataclass
+class Segment:
+    """One descriptor: a whole tensor or one shard segment of it (1-D views)."""
+    param: torch.Tensor
+    grad: torch.Tensor
+    q_m: torch.Tensor
+    q_w: torch.Tensor
+    param_id: int
+    row: int
+    slot: int
+    rng_offset: int = 0
+    u_m: torch.Tensor | None = None
+    u_w: torch.Tensor | None = None
+
+    def key(self) -> tuple:
+        return (self.param.data_ptr(), self.grad.data_ptr(), self.q_m.data_ptr(),
+                self.q_w.data_ptr(), self.param.numel(), self.param_id, self.row, self.slot,
+                self.rng_offset, self.param.dtype, self.grad.dtype,
+                0 if self.u_m is None else self.u_m.data_ptr(),
+                0 if self.u_w is None else self.u_w.data_ptr())
+
+
+def build_desc_table(segs: list[Segment]) -> tuple[np.ndarray, int]:
+    """numpy LumaTensorDesc table and the total octet count."""
+    n = len(segs)
+    d = np.zeros(n, dtype=DESC_DTYPE)
+    if n == 0:
+        return d, 0
+    d["param"] = [s.param.data_ptr() for s in segs]
+    d["grad"] = [s.grad.data_ptr() for s in segs]
+    d["q_m"] = [s.q_m.data_ptr() for s in segs]
+    d["q_w"] = [s.q_w.data_ptr() for s in segs]
+    d["u_m"] = [0 if s.u_m is None else s.u_m.data_ptr() for s in segs]
+    d["u_w"] = [0 if s.u_w is None else s.u_w.data_ptr() for s in segs]
+    numel = np.array([s.param.numel() for s in segs], dtype=np.int64)
+    octs = (numel + 7) // 8
+    d["numel"] = numel
+    d["oct_begin"] = np.concatenate([np.zeros(1, np.int64), np.cumsum(octs)[:-1]])
+    d["rng_offset"] = [s.rng_offset for s in segs]
+    d["param_id"] = [s.param_id for s in segs]
+    d["row"] = [s.row for s in segs]
+    d["slot"] = [s.slot for s in segs]
+    d["param_dtype"] = [dtype_code(s.param.dtype) for s in segs]
+    d["grad_dtype"] = [dtype_code(s.grad.dtype) for s in segs]
+    ptrs = np.stack([d["param"], d["grad"], d["q_m"], d["q_w"], d["u_m"], d["u_w"]])
+    d["vec_ok"] = np.all(ptrs % 16 == 0, axis=0).astype(np.uint8)
+    return d, int(octs.sum())
+
+
+class DeviceEngine:
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.n_slots = 0
+        self.slots = torch.zeros(0, dtype=torch.uint8, device=device)
+        self.rows_dev = torch.zeros(ROW_DTYPE.itemsize * 4, dtype=torch.uint8, device=device)
+        self._ring = []
+        self._ring_i = 0
+        self._sig = None
+        self._descs_dev = None
+        self._n_desc = 0
+        self._total_oct = 0
+        self._args = _lib.LumaStepArgs()
+
+    # -- slots ---------------------------------------------------------------
+    def ensure_slots(self, n: int) -> None:
+        if n <= self.n_slots:
+            return
+        cap = max(n, 2 * self.n_slots, 16)
+        new = torch.zeros(cap * SLOT_DTYPE.itemsize, dtype=torch.uint8, device=self.device)
+        if self.n_slots:
+            new[: self.slots.numel()].copy_(self.slots)
+        self.slots = new
+        self.n_slots = cap
+        self._sig = None  # slot base pointer changed
+
+    def write_grid(self, slot: int, parity: int, rec: np.ndarray) -> None:
+        """Store one LumaGrid into grid[parity] of `slot` (stream-ordered)."""
+        off = slot * SLOT_DTYPE.itemsize + parity * GRID_DTYPE.itemsize
+        src = torch.from_numpy(np.frombuffer(rec.tobytes(), dtype=np.uint8).copy())
+        self.slots[off: off + GRID_DTYPE.itemsize].copy_(src)
+
+    def reset_slot(self, slot: int) -> None:
+        off = slot * SLOT_DTYPE.itemsize
+        self.slots[off: off + SLOT_DTYPE.itemsize].zero_()
+
+    def read_slots(self) -> np.ndarray:
+        """All slots as a numpy LumaSlot array (synchronises the device)."""
+        host = self.slots.cpu().numpy()
+        return host.view(SLOT_DTYPE)
+
+    # -- per step ------------------------------------------------------------
+    def _upload_rows(self, rows: np.ndarray, stream: torch.cuda.Stream) -> None:
+        nbytes = rows.nbytes
+        if self.rows_dev.numel() < nbytes:
+            self.rows_dev = torch.zeros(max(nbytes, 2 * self.rows_dev.numel()), dtype=torch.uint8,
+                                        device=self.device)
+        if not self._ring or self._ring[0][0].numel() < nbytes:
+            cap = max(nbytes, 64 * ROW_DTYPE.itemsize)
+            self._ring = [(torch.empty(cap, dtype=torch.uint8, pin_memory=True),
+                           torch.cuda.Event()) for _ in range(_RING)]
+            self._ring_i = 0
+        buf, ev = self._ring[self._ring_i]
+        self._ring_i = (self._ring_i + 1) % _RING
+        ev.synchronize()  # the copy that last read this buffer has executed
+        buf.numpy()[:nbytes] = np.frombuffer(rows.tobytes(), dtype=np.uint8)
+        with torch.cuda.stream(stream):
+            self.rows_dev[:nbytes].copy_(buf[:nbytes], non_blocking=True)
+            ev.record(stream)
+
+    def step(self, segs: list[Segment], rows: np.ndarray, base_seed: int,
+             stream: torch.cuda.Stream | None = None, events=None) -> None:
+        if not segs:
+            return
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        sig = tuple(s.key() for s in segs)
+        if sig != self._sig:
+            table, total = build_desc_table(segs)
+            self._descs_dev = torch.from_numpy(table.view(np.uint8).copy()).to(self.device)
+            self._n_desc = len(segs)
+            self._total_oct = total
+            self._sig = sig
+        self._upload_rows(rows, stream)
+        a = self._args
+        a.descs = self._descs_dev.data_ptr()
+        a.slots = self.slots.data_ptr()
+        a.rows = self.rows_dev.data_ptr()
+        a.n_desc = self._n_desc
+        a.n_rows = len(rows)
+        a.total_octets = self._total_oct
+        a.base_seed = ctypes.c_int64(int(base_seed)).value
+        for i in range(3):
+            a.events[i] = None if events is None else events[i]
+        _lib.check(_lib.lib().luma_step(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)),
+                   "luma_step")

@@ -1,0 +1,321 @@
+"""LUMA optimizer — ``torch.optim.Optimizer`` front end of the B200 backend.
+
+Drop-in for ``luma_optimizer.LUMA`` (IgorYashch/LUMA
+src/luma_optimizer/optimizer.py:39-524): same constructor, same per-parameter
+state (``step``, ``param_id``, ``Q_m``, ``Q_w`` int16, and ``S_m``/``S_v`` in
+``state_dict()``), same ``_base_seed`` seeding, same ``export_adamw_state`` /
+``import_adamw_state``.  The step itself runs as two sm_100a launches over
+every parameter at once (``libluma_b200.so``, reached through ctypes); there
+is no per-tensor Python work beyond validation and bookkeeping, no host
+synchronisation and no CPU fallback.
+
+Backends: ``"cuda"`` (this package) — ``"auto"`` and ``"triton"`` select it
+too, since it replaces the reference's Triton backend.  The reference's
+``"pytorch"`` backend is not part of this package.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+from torch.optim import Optimizer
+
+from . import _lib
+from .engine import DeviceEngine, Segment
+from .hostmath import SCALE_FLOOR_M, grid_record, precompute, rows_array, step_row
+
+_BACKENDS = {"auto", "cuda", "triton"}
+_PARAM_DTYPES = (torch.float32, torch.bfloat16)
+_GRAD_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+
+
+class LUMA(Optimizer):
+    r"""LUMA: Log-space Unbiased Momentum AdamW, B200 backend.
+
+    Parameters
+    ----------
+    params : iterable of parameters or parameter-group dicts.
+    lr : float, learning rate (default 1e-3).
+    betas : (float, float), EMA coefficients (default (0.9, 0.999)).
+    eps : float, denominator term (default 1e-8).
+    weight_decay : float, decoupled weight decay (default 0.01).
+    backend : "auto" | "cuda" | "triton" — all run the CUDA kernels.
+
+    Params may be float32 or bfloat16 (bf16 params are updated in float32
+    arithmetic and rounded once to bf16, nearest even); grads float32,
+    bfloat16 or float16.  All tensors must be contiguous CUDA tensors.
+
+    Stochastic rounding draws come from Philox4x32-10 keyed by
+    ``((step << 32) | 2*param_id) ^ _base_seed`` with the element index as
+    counter, so every rank with the same ``_base_seed`` produces the same
+    codes (DDP) and a checkpoint round trip resumes bit for bit.
+    """
+
+    def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 0.01, backend: str = "auto"):
+        # Validation order and messages follow optimizer.py:80-89.
+        if lr < 0.0:
+            raise ValueError(f"Invalid learning rate: {lr}")
+        if eps <= 0.0:
+            raise ValueError(f"Invalid epsilon: {eps}")
+        if not 0.0 <= betas[0] < 1.0:
+            raise ValueError(f"Invalid beta1: {betas[0]}")
+        if not 0.0 <= betas[1] < 1.0:
+            raise ValueError(f"Invalid beta2: {betas[1]}")
+        if weight_decay < 0.0:
+            raise ValueError(f"Invalid weight_decay: {weight_decay}")
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        # Same draw from the global torch RNG as optimizer.py:94-96, so ranks
+        # seeded identically share the quantization noise.
+        self._base_seed: int = int(
+            torch.randint(-(2 ** 63), 2 ** 63 - 1, (1,), dtype=torch.int64).item())
+        if backend not in _BACKENDS:
+            raise ValueError(f"Invalid backend: {backend}. Expected one of "
+                             f"{{'auto', 'cuda', 'triton'}} (this package runs the CUDA "
+                             f"backend; the reference's 'pytorch' backend is not included).")
+        self.backend = "cuda"
+        self._engines: dict[torch.device, DeviceEngine] = {}
+        self._slot_count: dict[torch.device, int] = {}
+        self._draw_hook = None
+        self._step_events = None  # optional (ev0, ev1, ev2) cudaEvent_t handles, timing hook
+
+    # ------------------------------------------------------------------
+    # helpers
+    # ------------------------------------------------------------------
+    @staticmethod
+    def _unwrap_tensor(t):
+        """DTensor (FSDP2) -> local shard (optimizer.py:399-407)."""
+        if t is None:
+            return None
+        if hasattr(t, "_local_tensor"):
+            return t._local_tensor
+        return t
+
+    def _engine(self, device: torch.device) -> DeviceEngine:
+        eng = self._engines.get(device)
+        if eng is None:
+            _lib.lib()  # fail loudly here if the library is missing
+            eng = DeviceEngine(device)
+            self._engines[device] = eng
+            self._slot_count[device] = 0
+        return eng
+
+    def _new_slot(self, device: torch.device) -> int:
+        eng = self._engine(device)
+        k = self._slot_count[device]
+        self._slot_count[device] = k + 1
+        eng.ensure_slots(k + 1)
+        return k
+
+    def _set_draw_hook(self, fn) -> None:
+        """Test hook: ``fn(param_id, step, param) -> (u_m, u_w)`` float32 CUDA
+        tensors with param's numel replace the Philox uniforms (the kernels'
+        injected-draw path).  ``None`` restores Philox."""
+        self._draw_hook = fn
+
+    def _grid_scales(self) -> dict[int, tuple[float, float]]:
+        """(S_m, S_v) per state-holding param, read from the device slots."""
+        out = {}
+        host = {dev: eng.read_slots() for dev, eng in self._engines.items()}
+        for group in self.param_groups:
+            for p in group["params"]:
+                st = self.state.get(p)
+                if not st or "_slot" not in st:
+                    continue
+                param = self._unwrap_tensor(p)
+                g = host[param.device][st["_slot"]]["grid"][st["step"] & 1]
+                out[id(p)] = (float(g["S_m"]), float(g["S_v"]))
+        return out
+
+    # ------------------------------------------------------------------
+    # checkpointing (optimizer.py:119-183)
+    # ------------------------------------------------------------------
+    def state_dict(self) -> dict:
+        """Portable state dict: per param ``step, param_id, Q_m, Q_w, S_m, S_v``
+        plus top-level ``_base_seed``; no private (``_``) keys."""
+        scales = self._grid_scales()
+        raw = super().state_dict()
+        by_index = {}
+        idx = 0
+        for group in self.param_groups:
+            for p in group["params"]:
+                by_index[idx] = p
+                idx += 1
+        clean = {}
+        for k, s in raw["state"].items():
+            cs = {key: v for key, v in s.items() if not key.startswith("_")}
+            p = by_index.get(k)
+            if p is not None and id(p) in scales:
+                cs["S_m"], cs["S_v"] = scales[id(p)]
+            clean[k] = cs
+        raw["state"] = clean
+        raw["_base_seed"] = self._base_seed
+        return raw
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        """Load a state dict written by this backend or by the reference.
+
+        Q_m/Q_w are kept as int16 codes (torch's loader would cast them to the
+        param dtype); S_m/S_v move into the device slot of each param.
+        """
+        self._base_seed = state_dict.get("_base_seed", self._base_seed)
+        sd = dict(state_dict)
+        sd["state"] = {k: dict(v) for k, v in state_dict["state"].items()}
+        codes = {}
+        for k, s in sd["state"].items():
+            codes[k] = {key: s.pop(key) for key in ("Q_m", "Q_w") if key in s}
+        saved_ids = [i for g in sd["param_groups"] for i in g["params"]]
+        super().load_state_dict(sd)
+        params = [p for g in self.param_groups for p in g["params"]]
+        pmap = dict(zip(saved_ids, params))
+        eps_of = {id(p): g["eps"] for g in self.param_groups for p in g["params"]}
+        for k, cd in codes.items():
+            p = pmap.get(int(k) if isinstance(k, str) else k)
+            if p is None:
+                continue
+            st = self.state[p]
+            param = self._unwrap_tensor(p)
+            for key, v in cd.items():
+                st[key] = v.to(device=param.device).to(torch.int16)
+        for p in params:
+            st = self.state.get(p)
+            if not st or "S_m" not in st:
+                continue
+            param = self._unwrap_tensor(p)
+            if not param.is_cuda:
+                continue
+            slot = st.get("_slot")
+            if slot is None:
+                slot = self._new_slot(param.device)
+                st["_slot"] = slot
+            eng = self._engine(param.device)
+            eng.reset_slot(slot)
+            eng.write_grid(slot, st["step"] & 1, grid_record(st["S_m"], st["S_v"], eps_of[id(p)]))
+            st.pop("S_m")
+            st.pop("S_v")
+
+    # ------------------------------------------------------------------
+    # AdamW interop (optimizer.py:189-335)
+    # ------------------------------------------------------------------
+    def export_adamw_state(self) -> dict:
+        """Decoded float32 ``exp_avg`` / ``exp_avg_sq`` in torch.optim.AdamW layout."""
+        scales = self._grid_scales()
+        param_to_idx = {}
+        idx = 0
+        for group in self.param_groups:
+            for p in group["params"]:
+                param_to_idx[id(p)] = idx
+                idx += 1
+        adamw_state = {}
+        for group in self.param_groups:
+            eps = group["eps"]
+            for p in group["params"]:
+                st = self.state.get(p)
+                if not st:
+                    continue
+                S_m, S_v = scales[id(p)] if id(p) in scales else (st["S_m"], st["S_v"])
+                w_min, delta_m, _, delta_w, _ = precompute(S_m, S_v, eps)
+                q_m, q_w = st["Q_m"], st["Q_w"]
+                exp_avg = torch.empty(q_m.shape, dtype=torch.float32, device=q_m.device)
+                exp_avg_sq = torch.empty(q_m.shape, dtype=torch.float32, device=q_m.device)
+                if q_m.numel():
+                    stream = torch.cuda.current_stream(q_m.device)
+                    _lib.check(_lib.lib().luma_decode(
+                        q_m.data_ptr(), q_w.data_ptr(), q_m.numel(),
+                        float(np.float32(delta_m)), float(np.float32(w_min)),
+                        float(np.float32(delta_w)), float(np.float32(eps)),
+                        exp_avg.data_ptr(), exp_avg_sq.data_ptr(),
+                        ctypes.c_void_p(stream.cuda_stream)), "luma_decode")
+                adamw_state[param_to_idx[id(p)]] = {
+                    "step": torch.tensor(float(st["step"])),
+                    "exp_avg": exp_avg,
+                    "exp_avg_sq": exp_avg_sq,
+                }
+        param_groups = []
+        for group in self.param_groups:
+            pg = {k: v for k, v in group.items() if k != "params"}
+            pg["params"] = [param_to_idx[id(p)] for p in group["params"]]
+            param_groups.append(pg)
+        return {"state": adamw_state, "param_groups": param_groups}
+
+    # ------------------------------------------------------------------
+    # step (optimizer.py:413-524)
+    # ------------------------------------------------------------------
+    @torch.no_grad()
+    def step(self, closure=None):
+        """One optimisation step for every parameter with a gradient."""
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+
+        # Pass A: validate everything before touching any state.
+        work = []
+        param_idx = 0
+        for gi, group in enumerate(self.param_groups):
+            for p in group["params"]:
+                param_idx += 1
+                if p.grad is None:
+                    continue
+                param = self._unwrap_tensor(p)
+                grad = self._unwrap_tensor(p.grad)
+                if param.numel() == 0:
+                    continue  # empty FSDP shard on this rank
+                if grad.is_sparse:
+                    raise RuntimeError("LUMA does not support sparse gradients")
+                if param.dtype not in _PARAM_DTYPES:
+                    raise ValueError(
+                        f"LUMA requires float32 or bfloat16 parameters (got {param.dtype}).")
+                if grad.dtype not in _GRAD_DTYPES:
+                    raise ValueError(f"LUMA requires float32/bfloat16/float16 gradients "
+                                     f"(got {grad.dtype}).")
+                if not param.is_cuda:
+                    raise RuntimeError(
+                        f"LUMA backend 'cuda' requires CUDA tensors (param on {param.device}).")
+                if grad.device != param.device:
+                    raise ValueError("LUMA requires the gradient on the parameter's device")
+                if grad.shape != param.shape:
+                    raise ValueError("LUMA requires the gradient to have the parameter's shape")
+                if not param.is_contiguous():
+                    raise ValueError("LUMA CUDA kernel requires contiguous parameters")
+                if not grad.is_contiguous():
+                    raise ValueError("LUMA CUDA kernel requires contiguous gradients")
+                work.append((p, param, grad, gi, param_idx - 1))
+
+        # Pass B: state bookkeeping and per-device segment lists.
+        per_dev: dict[torch.device, tuple[list[Segment], dict]] = {}
+        for p, param, grad, gi, pidx in work:
+            state = self.state[p]
+            if len(state) == 0:
+                state["step"] = 0
+                state["param_id"] = pidx
+            state["step"] += 1
+            t = state["step"]
+            if t == 1:
+                state["Q_m"] = torch.empty_like(param, dtype=torch.int16)
+                state["Q_w"] = torch.empty_like(param, dtype=torch.int16)
+            if "_slot" not in state:
+                state["_slot"] = self._new_slot(param.device)
+            segs, rowmap = per_dev.setdefault(param.device, ([], {}))
+            row = rowmap.setdefault((gi, t), len(rowmap))
+            seg = Segment(param.view(-1), grad.view(-1), state["Q_m"].view(-1),
+                          state["Q_w"].view(-1), state["param_id"], row, state["_slot"])
+            if self._draw_hook is not None:
+                um, uw = self._draw_hook(state["param_id"], t, param)
+                seg.u_m = um.reshape(-1)
+                seg.u_w = uw.reshape(-1)
+            segs.append(seg)
+
+        for dev, (segs, rowmap) in per_dev.items():
+            rows = [None] * len(rowmap)
+            for (gi, t), r in rowmap.items():
+                g = self.param_groups[gi]
+                rows[r] = step_row(t, g["lr"], g["betas"][0], g["betas"][1], g["eps"],
+                                   g["weight_decay"])
+            self._engine(dev).step(segs, rows_array(rows), self._base_seed,
+                                   events=self._step_events)
+        return loss

@@ -1,0 +1,196 @@
+"""Parity of the CUDA backend with the reference algorithm (GPU).
+
+Bit-exact bar: the oracle (``oracle/luma_ref.py``, the reference's op
+sequence) run on CUDA tensors of the same B200 is what the reference's
+PyTorch backend computes there.  Fed the same uniforms, the CUDA backend must
+produce identical params, Q_m, Q_w and S_m/S_v at every step — with the
+golden fixtures' injected uniforms, and with the backend's own Philox stream
+(``oracle/philox.py`` restates it on the host).
+
+Tolerance bar (cross-device): against the CPU reference goldens the GPU's
+libm and CUDA's "tensor / scalar = tensor * fl32(1/scalar)" rule differ in the
+last bit, so codes may move by one grid bin and params by a few ulp.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import GoldenCase, case_names
+from oracle import philox
+from oracle.luma_ref import OracleLUMA, decode_momentum, decode_preconditioner, precompute
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _luma():
+    from luma_b200 import LUMA
+    return LUMA
+
+
+def _index_map(groups):
+    return {id(p): k for k, p in enumerate(p for g in groups for p in g["params"])}
+
+
+def _assert_same_state(tag, opt, oracle, params, groups):
+    sd = opt.state_dict()["state"]
+    idx = _index_map(groups)
+    for i, p in enumerate(params):
+        st = opt.state.get(p)
+        ost = oracle.state.get(id(p))
+        assert (not st) == (not ost), f"{tag} param {i}: state presence differs"
+        if not st:
+            continue
+        assert torch.equal(st["Q_m"], ost["Q_m"]), f"{tag} param {i}: Q_m differs ({(st['Q_m'] != ost['Q_m']).sum().item()} elems)"
+        assert torch.equal(st["Q_w"], ost["Q_w"]), f"{tag} param {i}: Q_w differs ({(st['Q_w'] != ost['Q_w']).sum().item()} elems)"
+        s = sd[idx[id(p)]]
+        assert (s["S_m"], s["S_v"]) == (ost["S_m"], ost["S_v"]), f"{tag} param {i}: scales differ"
+        assert s["step"] == ost["step"]
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_golden_injected_bit_exact_vs_oracle_cuda(name):
+    """Golden inputs and uniforms: CUDA kernels == reference op sequence on CUDA."""
+    LUMA = _luma()
+    case = GoldenCase(name)
+    pk = case.make_params(DEV)
+    po = case.make_params(DEV)
+    gk, go = case.groups(pk), case.groups(po)
+    opt = LUMA(gk)
+    cur = {}
+    opt._set_draw_hook(lambda pid, t, like: cur[pid])
+    orc = OracleLUMA(go, draws=lambda pid, t, like: cur[pid])
+    for s in range(1, case.steps + 1):
+        case.set_grads(pk, s)
+        case.set_grads(po, s)
+        cur.clear()
+        cur.update(case.draws(s, DEV))
+        opt.step()
+        orc.step()
+        for i, (a, b) in enumerate(zip(pk, po)):
+            assert torch.equal(a.detach(), b.detach()), (
+                f"{name} step {s} param {i}: {(a != b).sum().item()} elements differ")
+        _assert_same_state(f"{name} step {s}", opt, orc, pk, gk)
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_golden_cross_device_tolerance(name):
+    """CUDA backend vs the CPU reference goldens: params within rtol 1e-6
+    after step 1 and codes within one grid bin at every step."""
+    LUMA = _luma()
+    case = GoldenCase(name)
+    pk = case.make_params(DEV)
+    opt = LUMA(case.groups(pk))
+    cur = {}
+    opt._set_draw_hook(lambda pid, t, like: cur[pid])
+    for s in range(1, case.steps + 1):
+        case.set_grads(pk, s)
+        cur.clear()
+        cur.update(case.draws(s, DEV))
+        opt.step()
+        for i, p in enumerate(pk):
+            exp = case.expected(s, i)
+            got = p.detach().float().cpu()
+            want = exp["p"].float()
+            if s == 1:
+                tol = 1e-6 * want.abs().max().item() + 1e-12
+                if p.dtype == torch.bfloat16:
+                    tol = max(tol, 2 ** -7 * want.abs().max().item())
+                assert (got - want).abs().max().item() <= tol, (name, s, i)
+            if "qm" in exp:
+                st = opt.state[p]
+                dq_m = (st["Q_m"].cpu().int().reshape(-1) - exp["qm"].int().reshape(-1)).abs()
+                qw_k = st["Q_w"].cpu().int().reshape(-1) & 0xFFFF
+                qw_r = exp["qw"].int().reshape(-1) & 0xFFFF
+                dq_w = (qw_k - qw_r).abs()
+                lim = 1 if s == 1 else 2 * s
+                assert dq_m.max().item() <= lim, (name, s, i, dq_m.max().item())
+                assert dq_w.max().item() <= lim, (name, s, i, dq_w.max().item())
+
+
+def _philox_draws(opt):
+    def draws(pid, t, like):
+        seed = philox.step_seed(opt._base_seed, t, pid)
+        um, uw = philox.uniforms(seed, like.numel())
+        return (torch.from_numpy(um).reshape(like.shape).to(like.device),
+                torch.from_numpy(uw).reshape(like.shape).to(like.device))
+    return draws
+
+
+def _run_pair(shapes, pdt, gdts, steps, seed=0, gscale=1e-2, lr=1e-3, offsets=None):
+    """Step the CUDA backend (Philox) and the oracle (host Philox draws) side by side."""
+    LUMA = _luma()
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    pk, po = [], []
+    for k, shp in enumerate(shapes):
+        base = torch.randn(shp, generator=g) * 0.02
+        off = 0 if offsets is None else offsets[k]
+        if off:
+            # a view at an element offset: exercises the unaligned (scalar) path
+            buf = torch.zeros(base.numel() + off, dtype=pdt, device=DEV)
+            t = buf[off:].view(shp)
+            t.copy_(base.to(pdt))
+        else:
+            t = base.to(pdt).to(DEV)
+        pk.append(t)
+        po.append(base.to(pdt).to(DEV))
+    for t in pk + po:
+        t.grad_dtype = None  # grads may differ in dtype from the param
+    opt = LUMA(pk, lr=lr)
+    orc = OracleLUMA(po, lr=lr, draws=_philox_draws(opt))
+    for s in range(steps):
+        for k, shp in enumerate(shapes):
+            gd = gdts[k % len(gdts)]
+            gr = (torch.randn(shp, generator=g) * gscale).to(gd).to(DEV)
+            pk[k].grad = gr.clone()
+            po[k].grad = gr.clone()
+        opt.step()
+        orc.step()
+        for k, (a, b) in enumerate(zip(pk, po)):
+            assert torch.equal(a.detach(), b.detach()), (
+                f"step {s + 1} tensor {k} {tuple(shapes[k])}: {(a != b).sum().item()} differ")
+        _assert_same_state(f"step {s + 1}", opt, orc, pk, [{"params": pk}])
+    return opt, pk
+
+
+@pytest.mark.parametrize("numel", [1, 7, 8, 9, 1023, 1025, 2048 * 3 + 5, (1 << 20) + 3])
+def test_philox_bit_exact_sizes(numel):
+    _run_pair([(numel,)], torch.float32, [torch.float32], steps=3)
+
+
+@pytest.mark.parametrize("pdt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16, torch.float16])
+def test_philox_bit_exact_dtypes(pdt, gdt):
+    _run_pair([(257, 129), (4096,)], pdt, [gdt], steps=3, gscale=1e-3)
+
+
+def test_unaligned_views_bit_exact():
+    shapes = [(1000,), (77, 13), (4096,)]
+    _run_pair(shapes, torch.float32, [torch.float32, torch.bfloat16], steps=3, offsets=[1, 3, 0])
+
+
+def test_ragged_many_tensors_bit_exact():
+    rng = np.random.default_rng(0)
+    sizes = [int(round(2 ** rng.uniform(0, 14))) for _ in range(300)]
+    _run_pair([(n,) for n in sizes], torch.float32, [torch.float32, torch.bfloat16], steps=2)
+
+
+def test_large_tensor_across_many_ctas_bit_exact():
+    """One tensor split over every CTA of the persistent grid plus small ones."""
+    _run_pair([(5_000_003,), (3,), (70_001,)], torch.bfloat16, [torch.bfloat16], steps=2, gscale=1e-3)
+
+
+def test_export_decode_bit_exact():
+    opt, pk = _run_pair([(3000,), (64, 64)], torch.float32, [torch.float32], steps=3)
+    exp = opt.export_adamw_state()
+    sd = opt.state_dict()
+    for k, p in enumerate(pk):
+        st = sd["state"][k]
+        w_min, delta_m, _, delta_w, _ = precompute(st["S_m"], st["S_v"], 1e-8)
+        m = decode_momentum(st["Q_m"], delta_m)
+        w = decode_preconditioner(st["Q_w"], w_min, delta_w)
+        v = (1.0 / w - 1e-8).clamp(min=0).square()
+        assert torch.equal(exp["state"][k]["exp_avg"], m)
+        assert torch.equal(exp["state"][k]["exp_avg_sq"], v)

@@ -1,0 +1,141 @@
+"""Host-side logic and the C ABI boundary — CPU (no GPU calls).
+
+* the shared library loads and exports every function include/luma_b200.h
+  declares; the ABI version and struct sizes agree with the Python mirrors;
+* every struct field offset in the header (compiled with gcc, offsetof)
+  equals the numpy mirror's offset;
+* host scalar math (grid precompute, per-step rows) reproduces the float32
+  roundings the reference's tensor ops apply to Python scalars;
+* descriptor-table construction (octet prefix sums, 128-bit alignment flag).
+"""
+
+import ctypes
+import math
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+from luma_b200 import _lib
+from luma_b200.engine import Segment, build_desc_table
+from luma_b200.hostmath import grid_record, precompute, step_row
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "luma_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(luma_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    h = _lib.lib()
+    names = declared_functions()
+    assert set(_lib.EXPORTED) <= set(names)
+    for n in names:
+        assert hasattr(h, n), f"{n} declared in luma_b200.h but not exported"
+
+
+def test_abi_version_and_struct_sizes():
+    h = _lib.lib()
+    assert h.luma_abi_version() == _lib.ABI_VERSION
+    out = (ctypes.c_int64 * 5)()
+    assert h.luma_struct_sizes(out, 5) == 5
+    assert tuple(out) == _lib.EXPECTED_SIZES
+    assert h.luma_last_error() == b""
+
+
+def test_invalid_arguments_rejected_without_gpu():
+    h = _lib.lib()
+    assert h.luma_step(None, None) == _lib.LUMA_ERR_INVALID
+    assert b"NULL" in h.luma_last_error()
+    a = _lib.LumaStepArgs()
+    a.n_desc = -1
+    assert h.luma_step(ctypes.byref(a), None) == _lib.LUMA_ERR_INVALID
+    a.n_desc = 0  # nothing to do: OK without touching the device
+    assert h.luma_step(ctypes.byref(a), None) == _lib.LUMA_OK
+    a.n_desc, a.total_octets, a.n_rows = 3, 10, 1
+    assert h.luma_step(ctypes.byref(a), None) == _lib.LUMA_ERR_INVALID  # NULL tables
+    assert h.luma_decode(None, None, -1, 0, 0, 0, 0, None, None, None) == _lib.LUMA_ERR_INVALID
+
+
+def _c_offsets(struct, fields, tmp_path):
+    src = tmp_path / "off.c"
+    body = "\n".join(f'  printf("%zu\\n", offsetof({struct}, {f}));' for f in fields)
+    src.write_text(f'#include <stddef.h>\n#include <stdio.h>\n#include "luma_b200.h"\n'
+                   f'int main(void) {{\n  printf("%zu\\n", sizeof({struct}));\n{body}\n  return 0;\n}}\n')
+    exe = tmp_path / "off"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
+                                           text=True).stdout.split()]
+    return vals[0], vals[1:]
+
+
+@pytest.mark.parametrize("struct,dtype", [("LumaTensorDesc", _lib.DESC_DTYPE),
+                                          ("LumaStepRow", _lib.ROW_DTYPE),
+                                          ("LumaGrid", _lib.GRID_DTYPE),
+                                          ("LumaSlot", _lib.SLOT_DTYPE)])
+def test_header_layout_matches_python_mirror(struct, dtype, tmp_path):
+    fields = list(dtype.names)
+    size, offs = _c_offsets(struct, fields, tmp_path)
+    assert size == dtype.itemsize
+    assert offs == [dtype.fields[f][1] for f in fields]
+
+
+def test_step_args_layout(tmp_path):
+    fields = [f for f, _ in _lib.LumaStepArgs._fields_]
+    size, offs = _c_offsets("LumaStepArgs", fields, tmp_path)
+    assert size == ctypes.sizeof(_lib.LumaStepArgs)
+    assert offs == [getattr(_lib.LumaStepArgs, f).offset for f in fields]
+
+
+def test_step_row_scalars():
+    f = np.float32
+    r = step_row(1, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+    assert r[0] == 1 and r[1] == 1e-8
+    assert r[2] == f(0.9) and r[3] == f(1.0 - 0.9) and r[4] == f(0.999) and r[5] == f(1.0 - 0.999)
+    assert r[6] == f(1.0 - 0.01 * 1e-3)
+    assert r[7] == f(-(1e-3 / (1.0 - 0.9)))
+    assert r[8] == f(1.0) / f(1.0 - 0.999)
+    assert r[9] == f(1e-8) and r[10] == f(1e8)
+    r7 = step_row(7, 3e-4, 0.9, 0.95, 1e-6, 0.1)
+    assert r7[7] == f(-(3e-4 / (1.0 - 0.9 ** 7)))
+    assert r7[8] == f(1.0) / f(1.0 - 0.95 ** 7)
+    r0 = step_row(3, 0.0, 0.9, 0.999, 1e-8, 0.0)
+    assert r0[6] == f(1.0) and r0[7] == 0.0 and math.copysign(1.0, r0[7]) == -1.0
+
+
+@pytest.mark.parametrize("S_m,S_v,eps", [(1e-9, 0.0, 1e-8), (0.5, 1e-6, 1e-8), (3.0, 2.5, 1e-8),
+                                         (1e4, 1e8, 1e-10), (1e-3, 1e-40, 1.0)])
+def test_grid_record(S_m, S_v, eps):
+    f = np.float32
+    g = grid_record(S_m, S_v, eps)
+    w_min, dm, z_m, dw, z_w = precompute(S_m, S_v, eps)
+    assert g["S_m"] == S_m and g["S_v"] == S_v and g["eps"] == eps
+    assert g["dm"] == f(dm) and g["inv_dm"] == f(1) / f(dm) and g["inv_zm"] == f(1) / f(z_m)
+    assert g["s_m32"] == f(S_m) and g["w_min"] == f(w_min) and g["inv_wmin"] == f(1) / f(w_min)
+    assert g["dw_pos"] == (dw > 0)
+    if dw > 0:
+        assert g["dw"] == f(dw) and g["inv_dw"] == f(1) / f(dw) and g["inv_zw"] == f(1) / f(z_w)
+    else:
+        assert g["dw"] == 0 and g["inv_zw"] == 1
+
+
+def test_desc_table_octets_and_alignment():
+    buf = torch.zeros(4096)
+    q = torch.zeros(8192, dtype=torch.int16)
+    segs = []
+    for k, (off, n) in enumerate([(0, 17), (64, 8), (129, 100), (512, 1)]):
+        segs.append(Segment(buf[off:off + n], buf[off:off + n], q[off:off + n], q[off:off + n],
+                            param_id=k, row=0, slot=k))
+    table, total = build_desc_table(segs)
+    assert list(table["numel"]) == [17, 8, 100, 1]
+    assert list(table["oct_begin"]) == [0, 3, 4, 17]
+    assert total == 18
+    assert list(table["vec_ok"]) == [1, 1, 0, 1]  # element offset 129 breaks 16-byte alignment
+    assert list(table["param_dtype"]) == [0] * 4 and list(table["slot"]) == [0, 1, 2, 3]
