@@ -110,7 +110,7 @@ typedef struct LumaStepRow {
   float   omb2;      /* fl32(1 - beta2)                                      */
   float   decay;     /* fl32(1 - weight_decay * lr)                          */
   float   neg_eta;   /* fl32(-(lr / (1 - beta1^t)))                          */
-  float   inv_bc2;   /* fl32(1 / fl32(1 - beta2^t)): tensor / scalar on CUDA */
+  float   inv_bc2;   /* fl32(1.0 / (1 - beta2^t)), float64 reciprocal       */
   float   eps32;     /* fl32(eps)                                            */
   float   w_max;     /* fl32(1 / eps)                                        */
   float   reserved;
@@ -118,21 +118,23 @@ typedef struct LumaStepRow {
 
 /*
  * One log grid (functional.py:74-92 evaluated for (S_m, S_v, eps)), with the
- * float32 values the element-wise code consumes.
+ * float32 values the element-wise code consumes.  A reference expression
+ * "tensor / s" with a Python float s is evaluated on CUDA as
+ * tensor * fl32(1.0 / s) (reciprocal in float64), hence the inv_* fields.
  */
 typedef struct LumaGrid {
   double  S_m;       /* max(max|m|, 1e-9), as the reference stores it       */
   double  S_v;       /* max(max v, 0)                                        */
   double  eps;       /* eps the float32 fields below were derived with      */
   float   dm;        /* fl32(delta_m)                                        */
-  float   inv_dm;    /* fl32(1 / fl32(delta_m))                              */
-  float   inv_zm;    /* fl32(1 / fl32(z_m))                                  */
+  float   inv_dm;    /* fl32(1.0 / delta_m)                                */
+  float   inv_zm;    /* fl32(1.0 / z_m)                                      */
   float   s_m32;     /* fl32(S_m) (momentum clamp)                           */
   float   w_min;     /* fl32(w_min)                                          */
-  float   inv_wmin;  /* fl32(1 / fl32(w_min))                                */
+  float   inv_wmin;  /* fl32(1.0 / w_min)                                    */
   float   dw;        /* fl32(delta_w)                                        */
-  float   inv_dw;    /* fl32(1 / fl32(delta_w)), 0 when delta_w == 0         */
-  float   inv_zw;    /* fl32(1 / fl32(z_w))                                  */
+  float   inv_dw;    /* fl32(1.0 / delta_w), 0 when delta_w == 0             */
+  float   inv_zw;    /* fl32(1.0 / z_w)                                      */
   int32_t dw_pos;    /* delta_w > 0                                          */
 } LumaGrid;          /* 64 bytes */
 

@@ -16,7 +16,8 @@
 //
 // Arithmetic follows the reference op by op as PyTorch's CUDA kernels execute
 // it (each op rounds to float32 on its own; a tensor divided by a Python
-// scalar is a multiply by the float32 reciprocal; addcdiv is one fma), so the
+// scalar s is a multiply by fl32(1.0 / s), the reciprocal taken in float64;
+// addcdiv is one fma), so the
 // codes and params are bit-identical to the reference running on CUDA when
 // both consume the same uniforms.  No fast-math: expm1f, expf, log1pf, logf,
 // IEEE division and sqrt are the CUDA library's accurate versions, the same
@@ -110,18 +111,17 @@ __device__ void make_grid(double S_m, double S_v, double eps, LumaGrid* g) {
   g->S_m = S_m;
   g->S_v = S_v;
   g->eps = eps;
-  const float dm = __double2float_rn(delta_m);
-  g->dm = dm;
-  g->inv_dm = __fdiv_rn(1.0f, dm);
-  g->inv_zm = __fdiv_rn(1.0f, __double2float_rn(z_m));
+  // A float32 tensor divided by a Python scalar s is multiplied by
+  // fl32(1.0 / s) on CUDA, the reciprocal taken in float64.
+  g->dm = __double2float_rn(delta_m);
+  g->inv_dm = __double2float_rn(1.0 / delta_m);
+  g->inv_zm = __double2float_rn(1.0 / z_m);
   g->s_m32 = __double2float_rn(S_m);
-  const float wmin = __double2float_rn(w_min);
-  g->w_min = wmin;
-  g->inv_wmin = __fdiv_rn(1.0f, wmin);
-  const float dw = __double2float_rn(delta_w);
-  g->dw = dw;
-  g->inv_dw = (delta_w > 0.0) ? __fdiv_rn(1.0f, dw) : 0.0f;
-  g->inv_zw = __fdiv_rn(1.0f, __double2float_rn(z_w));
+  g->w_min = __double2float_rn(w_min);
+  g->inv_wmin = __double2float_rn(1.0 / w_min);
+  g->dw = __double2float_rn(delta_w);
+  g->inv_dw = (delta_w > 0.0) ? __double2float_rn(1.0 / delta_w) : 0.0f;
+  g->inv_zw = __double2float_rn(1.0 / z_w);
   g->dw_pos = (delta_w > 0.0) ? 1 : 0;
 }
 
@@ -178,7 +178,7 @@ __device__ __forceinline__ void ema(const Consts& c, float g, float m, float v,
 }
 
 // param.mul_(1 - wd*lr); param.addcdiv_(m', sqrt(v'/bc2) + eps, value=-eta)
-// (functional.py:278-279, 213-214).  v'/bc2 is v' * fl32(1/fl32(bc2)) on
+// (functional.py:278-279, 213-214).  v'/bc2 is v' * fl32(1.0/bc2) on
 // CUDA; addcdiv is fma(value, m'/den, param).
 __device__ __forceinline__ float adamw(const Consts& c, float p, float mn, float vn) {
   const float pd = __fmul_rn(p, c.decay);
@@ -349,58 +349,131 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
   }
 }
 
-template <int PD, int GD>
-__device__ __forceinline__ void pass2_octets(const LumaTensorDesc& d, const Consts& c,
-                                             uint32_t k0, uint32_t k1,
-                                             int64_t o_lo, int64_t o_hi) {
-  const bool injected = d.u_m != nullptr;
-  for (int64_t o = o_lo + threadIdx.x; o < o_hi; o += kThreads) {
-    const int64_t e0 = o * 8;
-    const int64_t rem = d.numel - e0;
-    const int n = rem < 8 ? (int)rem : 8;
-    const bool vec = d.vec_ok != 0 && n == 8;  // 128-bit path only for full octets
-    float p[8], g[8];
-    load8<PD>(d.param, e0, n, vec, p);
-    load8<GD>(d.grad, e0, n, vec, g);
-    uint16_t qm[8], qw[8];
-    if (!c.init) {
-      load8_codes(d.q_m, e0, n, vec, qm);
-      load8_codes(d.q_w, e0, n, vec, qw);
-    }
-    float um[8], uw[8];
-    if (injected) {
-      load8_f32_plain(d.u_m, e0, n, vec, um);
-      load8_f32_plain(d.u_w, e0, n, vec, uw);
+// Two consecutive elements (one Philox block) of a stream as floats.
+template <int DT>
+__device__ __forceinline__ void load2(const void* base, int64_t e, bool both, bool vec,
+                                      float& x0, float& x1) {
+  if (DT == LUMA_F32) {
+    const float* p = static_cast<const float*>(base) + e;
+    if (vec) {
+      const float2 a = __ldcs(reinterpret_cast<const float2*>(p));
+      x0 = a.x; x1 = a.y;
     } else {
-      // element e draws Philox block ((rng_offset + e) / 2): words 0,1 for the
-      // even element of the pair, words 2,3 for the odd one (u_m, u_w).
-      const uint64_t pair0 = (uint64_t)(d.rng_offset + e0) >> 1;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint64_t ctr = pair0 + k;
-        const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
-        um[2 * k] = u24(r.x);
-        uw[2 * k] = u24(r.y);
-        um[2 * k + 1] = u24(r.z);
-        uw[2 * k + 1] = u24(r.w);
-      }
+      x0 = p[0]; x1 = both ? p[1] : 0.0f;
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float m = 0.0f, v = 0.0f;
-      if (!c.init) {
-        m = decode_m((int)(int16_t)qm[j], c.o_dm);
-        v = decode_v((uint32_t)qw[j], c.o_wmin, c.o_dw, c.eps32);
-      }
-      float mn, vn;
-      ema(c, g[j], m, v, mn, vn);
-      p[j] = adamw(c, p[j], mn, vn);
-      qm[j] = (uint16_t)(int16_t)quant_m(c, mn, um[j]);
-      qw[j] = (uint16_t)quant_w(c, vn, uw[j]);
+  } else {
+    const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+    uint32_t h0, h1;
+    if (vec) {
+      const uint32_t a = __ldcs(reinterpret_cast<const unsigned int*>(p));
+      h0 = a & 0xFFFFu; h1 = a >> 16;
+    } else {
+      h0 = p[0]; h1 = both ? p[1] : 0u;
     }
-    store8<PD>(d.param, e0, n, vec, p);
-    store8_codes(d.q_m, e0, n, vec, qm);
-    store8_codes(d.q_w, e0, n, vec, qw);
+    if (DT == LUMA_BF16) {
+      x0 = __uint_as_float(h0 << 16);  // bf16 -> f32 is exact
+      x1 = __uint_as_float(h1 << 16);
+    } else {
+      x0 = __half2float(__ushort_as_half((unsigned short)h0));
+      x1 = __half2float(__ushort_as_half((unsigned short)h1));
+    }
+  }
+}
+
+__device__ __forceinline__ void load2_codes(const int16_t* base, int64_t e, bool both, bool vec,
+                                            uint32_t& q0, uint32_t& q1) {
+  const uint16_t* p = reinterpret_cast<const uint16_t*>(base) + e;
+  if (vec) {
+    const uint32_t a = __ldcs(reinterpret_cast<const unsigned int*>(p));
+    q0 = a & 0xFFFFu; q1 = a >> 16;
+  } else {
+    q0 = p[0]; q1 = both ? p[1] : 0u;
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void store2(void* base, int64_t e, bool both, bool vec, float x0, float x1) {
+  if (DT == LUMA_F32) {
+    float* p = static_cast<float*>(base) + e;
+    if (vec) {
+      __stcs(reinterpret_cast<float2*>(p), make_float2(x0, x1));
+    } else {
+      p[0] = x0;
+      if (both) p[1] = x1;
+    }
+  } else {  // bf16, round to nearest even
+    uint16_t* p = static_cast<uint16_t*>(base) + e;
+    const uint32_t h0 = __bfloat16_as_ushort(__float2bfloat16_rn(x0));
+    const uint32_t h1 = __bfloat16_as_ushort(__float2bfloat16_rn(x1));
+    if (vec) {
+      __stcs(reinterpret_cast<unsigned int*>(p), h0 | (h1 << 16));
+    } else {
+      p[0] = (uint16_t)h0;
+      if (both) p[1] = (uint16_t)h1;
+    }
+  }
+}
+
+__device__ __forceinline__ void store2_codes(int16_t* base, int64_t e, bool both, bool vec,
+                                             uint32_t q0, uint32_t q1) {
+  uint16_t* p = reinterpret_cast<uint16_t*>(base) + e;
+  if (vec) {
+    __stcs(reinterpret_cast<unsigned int*>(p), (q0 & 0xFFFFu) | (q1 << 16));
+  } else {
+    p[0] = (uint16_t)q0;
+    if (both) p[1] = (uint16_t)q1;
+  }
+}
+
+// One element of pass 2: decode, EMA, AdamW, re-quantize.
+__device__ __forceinline__ void pass2_elem(const Consts& c, float g, float& p, uint32_t& qm,
+                                           uint32_t& qw, float um, float uw) {
+  float m = 0.0f, v = 0.0f;
+  if (!c.init) {
+    m = decode_m((int)(int16_t)(uint16_t)qm, c.o_dm);
+    v = decode_v(qw, c.o_wmin, c.o_dw, c.eps32);
+  }
+  float mn, vn;
+  ema(c, g, m, v, mn, vn);
+  p = adamw(c, p, mn, vn);
+  qm = (uint32_t)(uint16_t)(int16_t)quant_m(c, mn, um);
+  qw = quant_w(c, vn, uw);
+}
+
+// Pass 2 over pairs [p_lo, p_hi) of a tensor: pair P holds elements 2P, 2P+1
+// and draws Philox block (rng_offset / 2 + P).
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Consts& c,
+                                            uint32_t k0, uint32_t k1, bool vec2,
+                                            int64_t p_lo, int64_t p_hi) {
+  const bool injected = d.u_m != nullptr;
+  const uint64_t ctr0 = (uint64_t)d.rng_offset >> 1;
+  for (int64_t P = p_lo + threadIdx.x; P < p_hi; P += kThreads) {
+    const int64_t e = 2 * P;
+    const bool both = e + 1 < d.numel;
+    const bool vec = vec2 && both;
+    float p0, p1, g0, g1;
+    uint32_t qm0 = 0, qm1 = 0, qw0 = 0, qw1 = 0;
+    load2<PD>(d.param, e, both, vec, p0, p1);
+    load2<GD>(d.grad, e, both, vec, g0, g1);
+    if (!c.init) {
+      load2_codes(d.q_m, e, both, vec, qm0, qm1);
+      load2_codes(d.q_w, e, both, vec, qw0, qw1);
+    }
+    float um0, um1, uw0, uw1;
+    if (injected) {
+      load2<LUMA_F32>(d.u_m, e, both, vec, um0, um1);
+      load2<LUMA_F32>(d.u_w, e, both, vec, uw0, uw1);
+    } else {
+      const uint64_t ctr = ctr0 + (uint64_t)P;
+      const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+      um0 = u24(r.x); uw0 = u24(r.y); um1 = u24(r.z); uw1 = u24(r.w);
+    }
+    pass2_elem(c, g0, p0, qm0, qw0, um0, uw0);
+    pass2_elem(c, g1, p1, qm1, qw1, um1, uw1);
+    store2<PD>(d.param, e, both, vec, p0, p1);
+    store2_codes(d.q_m, e, both, vec, qm0, qm1);
+    store2_codes(d.q_w, e, both, vec, qw0, qw1);
   }
 }
 
@@ -520,17 +593,25 @@ __global__ void __launch_bounds__(kThreads) luma_pass_kernel(const LumaStepArgs 
       const uint64_t seed = ((uint64_t)s.row.step << 32 | (uint64_t)((int64_t)d.param_id * 2)) ^
                             (uint64_t)a.base_seed;
       const uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+      const int64_t n_pairs = (d.numel + 1) / 2;
+      const int64_t p_lo = 4 * o_lo;
+      const int64_t p_hi = min(4 * o_hi, n_pairs);
+      const int pes = d.param_dtype == LUMA_F32 ? 8 : 4;   // bytes of a param pair
+      const int ges = d.grad_dtype == LUMA_F32 ? 8 : 4;
+      const bool vec2 = ((uintptr_t)d.param % pes == 0) && ((uintptr_t)d.grad % ges == 0) &&
+                        ((uintptr_t)d.q_m % 4 == 0) && ((uintptr_t)d.q_w % 4 == 0) &&
+                        ((uintptr_t)d.u_m % 8 == 0) && ((uintptr_t)d.u_w % 8 == 0);
       if (d.param_dtype == LUMA_F32) {
         switch (d.grad_dtype) {
-          case LUMA_F32: pass2_octets<LUMA_F32, LUMA_F32>(d, c, k0, k1, o_lo, o_hi); break;
-          case LUMA_BF16: pass2_octets<LUMA_F32, LUMA_BF16>(d, c, k0, k1, o_lo, o_hi); break;
-          default: pass2_octets<LUMA_F32, LUMA_F16>(d, c, k0, k1, o_lo, o_hi); break;
+          case LUMA_F32: pass2_pairs<LUMA_F32, LUMA_F32>(d, c, k0, k1, vec2, p_lo, p_hi); break;
+          case LUMA_BF16: pass2_pairs<LUMA_F32, LUMA_BF16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
+          default: pass2_pairs<LUMA_F32, LUMA_F16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
         }
       } else {
         switch (d.grad_dtype) {
-          case LUMA_F32: pass2_octets<LUMA_BF16, LUMA_F32>(d, c, k0, k1, o_lo, o_hi); break;
-          case LUMA_BF16: pass2_octets<LUMA_BF16, LUMA_BF16>(d, c, k0, k1, o_lo, o_hi); break;
-          default: pass2_octets<LUMA_BF16, LUMA_F16>(d, c, k0, k1, o_lo, o_hi); break;
+          case LUMA_F32: pass2_pairs<LUMA_BF16, LUMA_F32>(d, c, k0, k1, vec2, p_lo, p_hi); break;
+          case LUMA_BF16: pass2_pairs<LUMA_BF16, LUMA_BF16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
+          default: pass2_pairs<LUMA_BF16, LUMA_F16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
         }
       }
     }

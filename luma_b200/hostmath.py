@@ -8,7 +8,8 @@ float32 roundings its tensor ops apply to Python scalars:
   ``math``, float64);
 * ``grid_record`` turns it into the float32 values the kernels consume — a
   Python scalar multiplying a float32 tensor is rounded to float32, and on
-  CUDA ``tensor / scalar`` is ``tensor * fl32(1 / fl32(scalar))``;
+  CUDA ``tensor / scalar`` is ``tensor * fl32(1.0 / scalar)`` (the reciprocal
+  taken in float64, then rounded once to float32);
 * ``step_row`` holds the per-step scalars of functional.py:262-264 and
   optimizer.py:423-426.
 """
@@ -40,9 +41,10 @@ def precompute(S_m: float, S_v: float, eps: float) -> tuple[float, float, float,
 
 
 def _inv32(x: float) -> np.float32:
-    """fl32(1 / fl32(x)): how a CUDA tensor is divided by a Python scalar."""
-    with np.errstate(divide="ignore", over="ignore"):
-        return _f32(1.0) / _f32(x)
+    """fl32(1.0 / x), reciprocal in float64: the factor a CUDA float32 tensor is
+    multiplied by when it is divided by the Python scalar x."""
+    with np.errstate(over="ignore"):
+        return _f32(1.0 / x)
 
 
 def grid_record(S_m: float, S_v: float, eps: float) -> np.ndarray:

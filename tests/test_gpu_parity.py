@@ -34,12 +34,13 @@ def _index_map(groups):
     return {id(p): k for k, p in enumerate(p for g in groups for p in g["params"])}
 
 
-def _assert_same_state(tag, opt, oracle, params, groups):
+def _assert_same_state(tag, opt, oracle, params, oparams, groups):
+    """Kernel state of params[i] == oracle state of oparams[i] (codes, scales, step)."""
     sd = opt.state_dict()["state"]
     idx = _index_map(groups)
-    for i, p in enumerate(params):
+    for i, (p, op) in enumerate(zip(params, oparams)):
         st = opt.state.get(p)
-        ost = oracle.state.get(id(p))
+        ost = oracle.state.get(id(op))
         assert (not st) == (not ost), f"{tag} param {i}: state presence differs"
         if not st:
             continue
@@ -72,7 +73,7 @@ def test_golden_injected_bit_exact_vs_oracle_cuda(name):
         for i, (a, b) in enumerate(zip(pk, po)):
             assert torch.equal(a.detach(), b.detach()), (
                 f"{name} step {s} param {i}: {(a != b).sum().item()} elements differ")
-        _assert_same_state(f"{name} step {s}", opt, orc, pk, gk)
+        _assert_same_state(f"{name} step {s}", opt, orc, pk, po, gk)
 
 
 @pytest.mark.parametrize("name", case_names())
@@ -151,7 +152,7 @@ def _run_pair(shapes, pdt, gdts, steps, seed=0, gscale=1e-2, lr=1e-3, offsets=No
         for k, (a, b) in enumerate(zip(pk, po)):
             assert torch.equal(a.detach(), b.detach()), (
                 f"step {s + 1} tensor {k} {tuple(shapes[k])}: {(a != b).sum().item()} differ")
-        _assert_same_state(f"step {s + 1}", opt, orc, pk, [{"params": pk}])
+        _assert_same_state(f"step {s + 1}", opt, orc, pk, po, [{"params": pk}])
     return opt, pk
 
 

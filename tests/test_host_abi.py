@@ -101,11 +101,11 @@ def test_step_row_scalars():
     assert r[2] == f(0.9) and r[3] == f(1.0 - 0.9) and r[4] == f(0.999) and r[5] == f(1.0 - 0.999)
     assert r[6] == f(1.0 - 0.01 * 1e-3)
     assert r[7] == f(-(1e-3 / (1.0 - 0.9)))
-    assert r[8] == f(1.0) / f(1.0 - 0.999)
+    assert r[8] == f(1.0 / (1.0 - 0.999))
     assert r[9] == f(1e-8) and r[10] == f(1e8)
     r7 = step_row(7, 3e-4, 0.9, 0.95, 1e-6, 0.1)
     assert r7[7] == f(-(3e-4 / (1.0 - 0.9 ** 7)))
-    assert r7[8] == f(1.0) / f(1.0 - 0.95 ** 7)
+    assert r7[8] == f(1.0 / (1.0 - 0.95 ** 7))
     r0 = step_row(3, 0.0, 0.9, 0.999, 1e-8, 0.0)
     assert r0[6] == f(1.0) and r0[7] == 0.0 and math.copysign(1.0, r0[7]) == -1.0
 
@@ -117,11 +117,11 @@ def test_grid_record(S_m, S_v, eps):
     g = grid_record(S_m, S_v, eps)
     w_min, dm, z_m, dw, z_w = precompute(S_m, S_v, eps)
     assert g["S_m"] == S_m and g["S_v"] == S_v and g["eps"] == eps
-    assert g["dm"] == f(dm) and g["inv_dm"] == f(1) / f(dm) and g["inv_zm"] == f(1) / f(z_m)
-    assert g["s_m32"] == f(S_m) and g["w_min"] == f(w_min) and g["inv_wmin"] == f(1) / f(w_min)
+    assert g["dm"] == f(dm) and g["inv_dm"] == f(1 / dm) and g["inv_zm"] == f(1 / z_m)
+    assert g["s_m32"] == f(S_m) and g["w_min"] == f(w_min) and g["inv_wmin"] == f(1 / w_min)
     assert g["dw_pos"] == (dw > 0)
     if dw > 0:
-        assert g["dw"] == f(dw) and g["inv_dw"] == f(1) / f(dw) and g["inv_zw"] == f(1) / f(z_w)
+        assert g["dw"] == f(dw) and g["inv_dw"] == f(1 / dw) and g["inv_zw"] == f(1 / z_w)
     else:
         assert g["dw"] == 0 and g["inv_zw"] == 1
 
