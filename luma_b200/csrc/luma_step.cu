@@ -46,8 +46,18 @@ static_assert(sizeof(LumaSlot) == 144, "LumaSlot layout");
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kThreads = 256;           // luma_decode
+constexpr int kThreadsPass1 = 512;      // one CTA per SM (128 KB decode table)
+constexpr int kThreadsPass2 = 512;      // one CTA per SM, <= 128 registers
+constexpr int kMaxWarps = 32;
+
+// Decode table of expm1f(fl(|q| * delta_m)) for |q| = 0..32768, built in
+// shared memory when a CTA's segment of a tensor is long enough to repay the
+// 32769 expm1f evaluations.  Same function on the same inputs, so lookups are
+// bit-identical to evaluating expm1f.
+constexpr int kLutEntries = 32769;
+constexpr int64_t kLutMinElems = 131072;
+constexpr size_t kLutBytes = kLutEntries * sizeof(float);
 
 // ---------------------------------------------------------------------------
 // Error reporting
@@ -147,6 +157,11 @@ struct Consts {
   float n_sm32, n_dm, n_inv_dm, n_inv_zm, n_wmin, n_inv_wmin, n_dw, n_inv_dw, n_inv_zw;
   int n_dw_pos;
   int init;
+  // LogSR decision filter usable (delta small enough for the series)
+  bool series_m, series_w;
+  // pass-1 approximate decode
+  float o_dw_log2e;
+  float tau_v;  // kBoundEps * eps^2
 };
 
 // m = sgn(Q_m) * expm1(|Q_m| * delta_m)       functional.py:113-116
@@ -155,11 +170,16 @@ __device__ __forceinline__ float decode_m(int q, float dm) {
   return q < 0 ? -e : e;
 }
 
+__device__ __forceinline__ float decode_m_lut(int q, const float* lut) {
+  const float e = lut[abs(q)];
+  return q < 0 ? -e : e;
+}
+
 // w = w_min * exp(Q_w * delta_w)               functional.py:119-126
 // v = (1.0 / w - eps).clamp_min(0).square()    functional.py:270
 __device__ __forceinline__ float decode_v(uint32_t qu, float wmin, float dw, float eps32) {
   const float w = __fmul_rn(wmin, expf(__fmul_rn((float)qu, dw)));
-  const float t = clamp_min_keepnan(__fsub_rn(__fdiv_rn(1.0f, w), eps32), 0.0f);
+  const float t = clamp_min_keepnan(__fsub_rn(__frcp_rn(w), eps32), 0.0f);
   return __fmul_rn(t, t);
 }
 
@@ -186,14 +206,33 @@ __device__ __forceinline__ float adamw(const Consts& c, float p, float mn, float
   return __fmaf_rn(c.neg_eta, __fdiv_rn(mn, den), pd);
 }
 
+// LogSR decision  u < p*,  p* = fl(expm1f(fl(frac * delta)) * inv_z)
+// (functional.py:64-66).  For delta <= kSeriesMaxDelta the series
+// x + x^2/2 + x^3/6 (x = fl(frac * delta) <= delta) is within 3e-7 of p*:
+// expm1f is within 1 ulp, the omitted x^4/24 term is below 2e-9 relative,
+// and the roundings add under 2 ulp.  Only when u falls within kDecisionMargin
+// (6x that bound) of the series value is expm1f evaluated, so the decision,
+// and therefore the code, is the one the exact expression gives.
+constexpr float kSeriesMaxDelta = 0.01f;
+constexpr float kDecisionMargin = 0x1.0p-19f;
+
+__device__ __forceinline__ bool logsr_up(float fr, float delta, float inv_z, float u, bool series) {
+  const float x = __fmul_rn(fr, delta);
+  if (series) {
+    const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
+    const float diff = __fsub_rn(u, __fmul_rn(e, inv_z));
+    if (fabsf(diff) > kDecisionMargin) return diff < 0.0f;
+  }
+  return u < __fmul_rn(expm1f(x), inv_z);
+}
+
 // _quantize_momentum (functional.py:133-150) with _log_sr (functional.py:38-67).
 __device__ __forceinline__ int quant_m(const Consts& c, float mn, float u) {
   const float mc = clamp_keepnan(mn, -c.n_sm32, c.n_sm32);
   const float y = __fmul_rn(log1pf(fabsf(mc)), c.n_inv_dm);
   const float fy = floorf(y);
   const float fr = __fsub_rn(y, fy);
-  const float ps = __fmul_rn(expm1f(__fmul_rn(fr, c.n_dm)), c.n_inv_zm);
-  float r = __fadd_rn(fy, (u < ps) ? 1.0f : 0.0f);
+  float r = __fadd_rn(fy, logsr_up(fr, c.n_dm, c.n_inv_zm, u, c.series_m) ? 1.0f : 0.0f);
   r = clamp_keepnan(r, 0.0f, (float)LUMA_K_M);
   const float sg = (mc > 0.0f) ? 1.0f : ((mc < 0.0f) ? -1.0f : 0.0f);
   return (int)__fmul_rn(sg, r);
@@ -203,14 +242,60 @@ __device__ __forceinline__ int quant_m(const Consts& c, float mn, float u) {
 __device__ __forceinline__ uint32_t quant_w(const Consts& c, float vn, float u) {
   if (!c.n_dw_pos) return 0u;  // delta_w == 0: y = 0 and _log_sr returns 0
   const float den = __fadd_rn(__fsqrt_rn(clamp_min_keepnan(vn, 0.0f)), c.eps32);
-  const float w = clamp_keepnan(__fdiv_rn(1.0f, den), c.n_wmin, c.w_max);
+  const float w = clamp_keepnan(__frcp_rn(den), c.n_wmin, c.w_max);
   const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
   const float fy = floorf(y);
   const float fr = __fsub_rn(y, fy);
-  const float ps = __fmul_rn(expm1f(__fmul_rn(fr, c.n_dw)), c.n_inv_zw);
-  float r = __fadd_rn(fy, (u < ps) ? 1.0f : 0.0f);
+  float r = __fadd_rn(fy, logsr_up(fr, c.n_dw, c.n_inv_zw, u, c.series_w) ? 1.0f : 0.0f);
   r = clamp_keepnan(r, 0.0f, (float)LUMA_K_W);
   return (uint32_t)(int)r;  // .to(int32) then two's-complement wrap to int16
+}
+
+// ---------------------------------------------------------------------------
+// Pass-1 maxima with certified bounds.
+//
+// The new scales need the exact max |m'| and max v' of a tensor, but only the
+// maximal elements need their exact values.  Pass 1 evaluates every element
+// with a cheap approximate decode whose error is bounded (below), keeps a
+// running lower bound T of the maximum (warp-wide), and evaluates exactly only
+// elements whose upper bound exceeds both T and the exact maximum found so
+// far.  An element that is skipped has a value strictly below some other
+// element's exact value, so the exact maximum is unchanged.  NaN and
+// infinite approximations always take the exact path.
+//
+// Approximate decode, relative errors:
+//   expm1(x): x + x^2 (1/2 + x (1/6 + x/24)) for x < 0.125 (truncation < 2.1e-6),
+//             ex2.approx(x log2 e) - 1 otherwise (< 1e-5 up to x = 88.7, the
+//             largest |q| delta_m a float32 scale allows);
+//   v:        ex2.approx of an argument up to 128 (log2 of the grid ratio) with
+//             three roundings (< 1.6e-5), rcp.approx, then t = 1/w - eps:
+//             |v~ - v| < 2e-5 (v + t eps), t eps <= (v + eps^2) / 2.
+// Bounds, with kBoundEps = 2^-13 (>= 4x the errors above):
+//   | |m'~| - |m'| | <= kBoundEps (|beta1 m~| + |m'~|) + 2^-147   (q != 0)
+//   |  v'~ - v'    | <= kBoundEps  v'~ + kBoundEps eps^2 + 2^-147
+// The 2^-147 term covers roundings of subnormal intermediates.  For q == 0
+// (or beta1 == 0) m' = fl(c1 g) exactly and is taken as is.
+// ---------------------------------------------------------------------------
+
+constexpr float kBoundEps = 0x1.0p-13f;
+constexpr float kTinyAbs = 0x1.0p-147f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float expm1_approx(float x) {
+  const float series = __fmaf_rn(__fmul_rn(x, x),
+                                 __fmaf_rn(x, __fmaf_rn(x, 1.0f / 24.0f, 1.0f / 6.0f), 0.5f), x);
+  return x < 0.125f ? series : ex2_approx(x * 1.44269504f) - 1.0f;
 }
 
 // ---------------------------------------------------------------------------
@@ -315,37 +400,155 @@ __device__ __forceinline__ void store8_codes(int16_t* base, int64_t e0, int n, b
 // Per-tensor segment bodies
 // ---------------------------------------------------------------------------
 
-// Pass 1 body: returns this thread's max |m'| and max v' bit patterns.
+// Raw words of one octet of grad and codes (grad: 8 words for fp32, 4 for
+// 16-bit types; codes: 4 words each), kept packed for prefetching.
+struct RawOctet {
+  uint32_t g[8], qm[4], qw[4];
+};
+
+// Loads octet o (if o < o_hi) and returns its element count (0 if none).
 template <int GD>
-__device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Consts& c,
-                                             int64_t o_lo, int64_t o_hi,
-                                             uint32_t& am, uint32_t& av) {
-  for (int64_t o = o_lo + threadIdx.x; o < o_hi; o += kThreads) {
-    const int64_t e0 = o * 8;
-    const int64_t rem = d.numel - e0;
-    const int n = rem < 8 ? (int)rem : 8;
-    const bool vec = d.vec_ok != 0 && n == 8;  // 128-bit path only for full octets
-    float g[8];
-    load8<GD>(d.grad, e0, n, vec, g);
-    uint16_t qm[8], qw[8];
-    if (!c.init) {
-      load8_codes(d.q_m, e0, n, vec, qm);
-      load8_codes(d.q_w, e0, n, vec, qw);
+__device__ __forceinline__ int load_raw_octet(const LumaTensorDesc& d, int64_t o, int64_t o_hi,
+                                              RawOctet& r) {
+  if (o >= o_hi) return 0;
+  const int64_t e0 = o * 8;
+  const int64_t rem = d.numel - e0;
+  const int n = rem < 8 ? (int)rem : 8;
+  if (d.vec_ok != 0 && n == 8) {
+    if (GD == LUMA_F32) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(d.grad) + e0);
+      const uint4 a = __ldcs(p), b = __ldcs(p + 1);
+      r.g[0] = a.x; r.g[1] = a.y; r.g[2] = a.z; r.g[3] = a.w;
+      r.g[4] = b.x; r.g[5] = b.y; r.g[6] = b.z; r.g[7] = b.w;
+    } else {
+      const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(d.grad) + e0));
+      r.g[0] = a.x; r.g[1] = a.y; r.g[2] = a.z; r.g[3] = a.w;
     }
+    const uint4 m = __ldcs(reinterpret_cast<const uint4*>(d.q_m + e0));
+    const uint4 w = __ldcs(reinterpret_cast<const uint4*>(d.q_w + e0));
+    r.qm[0] = m.x; r.qm[1] = m.y; r.qm[2] = m.z; r.qm[3] = m.w;
+    r.qw[0] = w.x; r.qw[1] = w.y; r.qw[2] = w.z; r.qw[3] = w.w;
+  } else {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      if (j < n) {
-        float m = 0.0f, v = 0.0f;
-        if (!c.init) {
-          m = decode_m((int)(int16_t)qm[j], c.o_dm);
-          v = decode_v((uint32_t)qw[j], c.o_wmin, c.o_dw, c.eps32);
+      const bool in = j < n;
+      if (GD == LUMA_F32) {
+        r.g[j] = in ? static_cast<const uint32_t*>(d.grad)[e0 + j] : 0u;
+      } else {
+        const uint32_t h = in ? static_cast<const uint16_t*>(d.grad)[e0 + j] : 0u;
+        r.g[j >> 1] = (j & 1) ? (r.g[j >> 1] | (h << 16)) : h;
+      }
+      const uint32_t a = in ? (uint16_t)d.q_m[e0 + j] : 0u;
+      const uint32_t b = in ? (uint16_t)d.q_w[e0 + j] : 0u;
+      r.qm[j >> 1] = (j & 1) ? (r.qm[j >> 1] | (a << 16)) : a;
+      r.qw[j >> 1] = (j & 1) ? (r.qw[j >> 1] | (b << 16)) : b;
+    }
+  }
+  return n;
+}
+
+template <int GD>
+__device__ __forceinline__ void unpack8(const uint32_t (&w)[8], float (&x)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (GD == LUMA_F32) {
+      x[j] = __uint_as_float(w[j]);
+    } else {
+      const uint32_t h = (w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+      x[j] = (GD == LUMA_BF16) ? __uint_as_float(h << 16)
+                               : __half2float(__ushort_as_half((unsigned short)h));
+    }
+  }
+}
+
+// Pass 1 body: this thread's exact max |m'| and max v' bit patterns.  All
+// threads of the CTA run the same number of iterations (warp reductions).
+template <int GD>
+__device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Consts& c,
+                                             const float* lut, int64_t o_lo, int64_t o_hi,
+                                             uint32_t& am, uint32_t& av) {
+  constexpr int kThreads = kThreadsPass1;
+  if (c.init) {  // first step: m' = (1-b1) g, v' = (1-b2) g^2, cheap and exact
+    for (int64_t o = o_lo + threadIdx.x; o < o_hi; o += kThreads) {
+      const int64_t e0 = o * 8;
+      const int64_t rem = d.numel - e0;
+      const int n = rem < 8 ? (int)rem : 8;
+      float g[8];
+      load8<GD>(d.grad, e0, n, d.vec_ok != 0 && n == 8, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < n) {
+          float mn, vn;
+          ema(c, g[j], 0.0f, 0.0f, mn, vn);
+          am = max(am, __float_as_uint(fabsf(mn)));
+          av = max(av, __float_as_uint(vn));
         }
-        float mn, vn;
-        ema(c, g[j], m, v, mn, vn);
-        am = max(am, __float_as_uint(fabsf(mn)));
-        av = max(av, __float_as_uint(vn));
       }
     }
+    return;
+  }
+  // Tm/Tv: warp-wide lower bounds of the maxima from earlier iterations;
+  // lm/lv: this thread's running lower bounds (they include the element
+  // under test, whose own bound never excludes it).  The next octet's raw
+  // words are loaded before the current octet is evaluated.
+  float Tm = 0.0f, Tv = 0.0f, lm = 0.0f, lv = 0.0f;
+  RawOctet cur;
+  int n_cur = load_raw_octet<GD>(d, o_lo + threadIdx.x, o_hi, cur);
+  for (int64_t ob = o_lo; ob < o_hi; ob += kThreads) {
+    RawOctet nxt;
+    const int n_nxt = load_raw_octet<GD>(d, ob + kThreads + threadIdx.x, o_hi, nxt);
+    const int n = n_cur;
+    if (n > 0) {
+      float g[8];
+      unpack8<GD>(cur.g, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < n) {
+          const int q = (int)(int16_t)(uint16_t)(cur.qm[j >> 1] >> (16 * (j & 1)));
+          const uint32_t qwj = (cur.qw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+          if (lut != nullptr) {
+            // exact |m'| from the decode table (functional.py:274, 282)
+            const float mne = __fadd_rn(__fmul_rn(c.beta1, decode_m_lut(q, lut)),
+                                        __fmul_rn(c.omb1, g[j]));
+            am = max(am, __float_as_uint(fabsf(mne)));
+          } else if (q == 0 || c.beta1 == 0.0f) {
+            // fl(beta1 * 0) = 0, so m' = fl(c1 g) exactly
+            const float mne = fabsf(__fmul_rn(c.omb1, g[j]));
+            am = max(am, __float_as_uint(mne));
+            lm = fmaxf(lm, mne);
+          } else {
+            const float e = expm1_approx(__fmul_rn((float)abs(q), c.o_dm));
+            const float bm = c.beta1 * (q < 0 ? -e : e);
+            const float mn = fabsf(bm + c.omb1 * g[j]);
+            const float bnd_m = kBoundEps * (fabsf(bm) + mn) + kTinyAbs;
+            const float um = mn + bnd_m;
+            lm = fmaxf(lm, mn - bnd_m);
+            if (!(um <= __uint_as_float(am)) && !(um < fmaxf(Tm, lm))) {
+              // exact |m'| (functional.py:274, 282)
+              const float mx = decode_m(q, c.o_dm);
+              const float mne = __fadd_rn(__fmul_rn(c.beta1, mx), __fmul_rn(c.omb1, g[j]));
+              am = max(am, __float_as_uint(fabsf(mne)));
+            }
+          }
+          const float w = c.o_wmin * ex2_approx((float)qwj * c.o_dw_log2e);
+          const float t = fmaxf(rcp_approx(w) - c.eps32, 0.0f);
+          const float vn = c.beta2 * (t * t) + c.omb2 * (g[j] * g[j]);
+          const float bnd_v = kBoundEps * vn + c.tau_v;
+          const float uv = vn + bnd_v;
+          lv = fmaxf(lv, vn - bnd_v);
+          if (!(uv <= __uint_as_float(av)) && !(uv < fmaxf(Tv, lv))) {
+            // exact v' (functional.py:270, 275, 282)
+            const float v = decode_v(qwj, c.o_wmin, c.o_dw, c.eps32);
+            const float vne = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, __fmul_rn(g[j], g[j])));
+            av = max(av, __float_as_uint(vne));
+          }
+        }
+      }
+    }
+    Tm = fmaxf(Tm, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lm))));
+    Tv = fmaxf(Tv, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lv))));
+    cur = nxt;
+    n_cur = n_nxt;
   }
 }
 
@@ -426,11 +629,12 @@ __device__ __forceinline__ void store2_codes(int16_t* base, int64_t e, bool both
 }
 
 // One element of pass 2: decode, EMA, AdamW, re-quantize.
-__device__ __forceinline__ void pass2_elem(const Consts& c, float g, float& p, uint32_t& qm,
-                                           uint32_t& qw, float um, float uw) {
+__device__ __forceinline__ void pass2_elem(const Consts& c, const float* lut, float g, float& p,
+                                           uint32_t& qm, uint32_t& qw, float um, float uw) {
   float m = 0.0f, v = 0.0f;
   if (!c.init) {
-    m = decode_m((int)(int16_t)(uint16_t)qm, c.o_dm);
+    const int q = (int)(int16_t)(uint16_t)qm;
+    m = lut != nullptr ? decode_m_lut(q, lut) : decode_m(q, c.o_dm);
     v = decode_v(qw, c.o_wmin, c.o_dw, c.eps32);
   }
   float mn, vn;
@@ -440,26 +644,93 @@ __device__ __forceinline__ void pass2_elem(const Consts& c, float g, float& p, u
   qw = quant_w(c, vn, uw);
 }
 
+// Raw bits of one pair of every stream, as loaded (fp32: two words, 16-bit
+// types: one word).  Kept packed so the next pair can be prefetched while the
+// current one is computed, at a few registers' cost.
+struct RawPair {
+  uint32_t p[2], g[2], qm, qw;
+};
+
+template <int DT>
+__device__ __forceinline__ void raw2(const void* base, int64_t e, bool both, bool vec, uint32_t (&w)[2]) {
+  if (DT == LUMA_F32) {
+    const uint32_t* p = static_cast<const uint32_t*>(base) + e;
+    if (vec) {
+      const uint2 a = __ldcs(reinterpret_cast<const uint2*>(p));
+      w[0] = a.x; w[1] = a.y;
+    } else {
+      w[0] = p[0]; w[1] = both ? p[1] : 0u;
+    }
+  } else {
+    const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+    if (vec) {
+      w[0] = __ldcs(reinterpret_cast<const unsigned int*>(p));
+    } else {
+      w[0] = (uint32_t)p[0] | (both ? (uint32_t)p[1] << 16 : 0u);
+    }
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack2(const uint32_t (&w)[2], float& x0, float& x1) {
+  if (DT == LUMA_F32) {
+    x0 = __uint_as_float(w[0]); x1 = __uint_as_float(w[1]);
+  } else if (DT == LUMA_BF16) {
+    x0 = __uint_as_float(w[0] << 16);  // bf16 -> f32 is exact
+    x1 = __uint_as_float(w[0] & 0xFFFF0000u);
+  } else {
+    x0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xFFFFu)));
+    x1 = __half2float(__ushort_as_half((unsigned short)(w[0] >> 16)));
+  }
+}
+
+template <int PD, int GD>
+__device__ __forceinline__ void load_raw_pair(const LumaTensorDesc& d, bool init, bool vec2,
+                                              int64_t P, RawPair& r) {
+  const int64_t e = 2 * P;
+  const bool both = e + 1 < d.numel;
+  const bool vec = vec2 && both;
+  raw2<PD>(d.param, e, both, vec, r.p);
+  raw2<GD>(d.grad, e, both, vec, r.g);
+  r.qm = 0u;
+  r.qw = 0u;
+  if (!init) {
+    const uint16_t* qm = reinterpret_cast<const uint16_t*>(d.q_m) + e;
+    const uint16_t* qw = reinterpret_cast<const uint16_t*>(d.q_w) + e;
+    if (vec) {
+      r.qm = __ldcs(reinterpret_cast<const unsigned int*>(qm));
+      r.qw = __ldcs(reinterpret_cast<const unsigned int*>(qw));
+    } else {
+      r.qm = (uint32_t)qm[0] | (both ? (uint32_t)qm[1] << 16 : 0u);
+      r.qw = (uint32_t)qw[0] | (both ? (uint32_t)qw[1] << 16 : 0u);
+    }
+  }
+}
+
 // Pass 2 over pairs [p_lo, p_hi) of a tensor: pair P holds elements 2P, 2P+1
-// and draws Philox block (rng_offset / 2 + P).
+// and draws Philox block (rng_offset / 2 + P).  The next pair's loads are
+// issued before the current pair is computed.
 template <int PD, int GD>
 __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Consts& c,
-                                            uint32_t k0, uint32_t k1, bool vec2,
+                                            const float* lut, uint32_t k0, uint32_t k1, bool vec2,
                                             int64_t p_lo, int64_t p_hi) {
+  constexpr int kThreads = kThreadsPass2;
   const bool injected = d.u_m != nullptr;
   const uint64_t ctr0 = (uint64_t)d.rng_offset >> 1;
-  for (int64_t P = p_lo + threadIdx.x; P < p_hi; P += kThreads) {
+  int64_t P = p_lo + threadIdx.x;
+  RawPair cur;
+  if (P < p_hi) load_raw_pair<PD, GD>(d, c.init, vec2, P, cur);
+  for (; P < p_hi; P += kThreads) {
+    RawPair nxt;
+    if (P + kThreads < p_hi) load_raw_pair<PD, GD>(d, c.init, vec2, P + kThreads, nxt);
     const int64_t e = 2 * P;
     const bool both = e + 1 < d.numel;
     const bool vec = vec2 && both;
     float p0, p1, g0, g1;
-    uint32_t qm0 = 0, qm1 = 0, qw0 = 0, qw1 = 0;
-    load2<PD>(d.param, e, both, vec, p0, p1);
-    load2<GD>(d.grad, e, both, vec, g0, g1);
-    if (!c.init) {
-      load2_codes(d.q_m, e, both, vec, qm0, qm1);
-      load2_codes(d.q_w, e, both, vec, qw0, qw1);
-    }
+    unpack2<PD>(cur.p, p0, p1);
+    unpack2<GD>(cur.g, g0, g1);
+    uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
+    uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
     float um0, um1, uw0, uw1;
     if (injected) {
       load2<LUMA_F32>(d.u_m, e, both, vec, um0, um1);
@@ -469,11 +740,12 @@ __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Const
       const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
       um0 = u24(r.x); uw0 = u24(r.y); um1 = u24(r.z); uw1 = u24(r.w);
     }
-    pass2_elem(c, g0, p0, qm0, qw0, um0, uw0);
-    pass2_elem(c, g1, p1, qm1, qw1, um1, uw1);
+    pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
+    pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
     store2<PD>(d.param, e, both, vec, p0, p1);
     store2_codes(d.q_m, e, both, vec, qm0, qm1);
     store2_codes(d.q_w, e, both, vec, qw0, qw1);
+    cur = nxt;
   }
 }
 
@@ -509,6 +781,11 @@ __device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Cons
     c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
     c.n_wmin = s.enc.w_min; c.n_inv_wmin = s.enc.inv_wmin; c.n_dw = s.enc.dw;
     c.n_inv_dw = s.enc.inv_dw; c.n_inv_zw = s.enc.inv_zw; c.n_dw_pos = s.enc.dw_pos;
+    c.series_m = c.n_dm <= kSeriesMaxDelta;
+    c.series_w = c.n_dw <= kSeriesMaxDelta;
+  } else {
+    c.o_dw_log2e = c.o_dw * 1.44269504f;
+    c.tau_v = kBoundEps * c.eps32 * c.eps32 + kTinyAbs;
   }
 }
 
@@ -528,10 +805,14 @@ __device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShare
 }
 
 template <bool PASS2>
-__global__ void __launch_bounds__(kThreads) luma_pass_kernel(const LumaStepArgs a) {
+__global__ void __launch_bounds__(PASS2 ? kThreadsPass2 : kThreadsPass1, 1)
+luma_pass_kernel(const LumaStepArgs a, const int lut_ok) {
+  constexpr int kThreads = PASS2 ? kThreadsPass2 : kThreadsPass1;
+  constexpr int kWarps = kThreads / 32;
   __shared__ SegShared s;
-  __shared__ uint32_t red_m[kWarps], red_v[kWarps];
+  __shared__ uint32_t red_m[kMaxWarps], red_v[kMaxWarps];
   __shared__ int s_di;
+  extern __shared__ float s_lut[];  // kLutEntries floats when launched with the table
 
   const int64_t T = a.total_octets;
   const int64_t lo = (T * (int64_t)blockIdx.x) / (int64_t)gridDim.x;
@@ -551,13 +832,21 @@ __global__ void __launch_bounds__(kThreads) luma_pass_kernel(const LumaStepArgs 
     const int64_t o_hi = min(hi - d.oct_begin, n_oct);
     Consts c;
     fill_consts(s, PASS2, c);
+    // Decode table for long segments of quantized (t >= 2) tensors.
+    const float* lut = nullptr;
+    if (lut_ok && !c.init && (o_hi - o_lo) * 8 >= kLutMinElems) {
+      for (int i = threadIdx.x; i < kLutEntries; i += kThreads)
+        s_lut[i] = expm1f(__fmul_rn((float)i, c.o_dm));
+      __syncthreads();
+      lut = s_lut;
+    }
 
     if (!PASS2) {
       uint32_t am = 0u, av = 0u;
       switch (d.grad_dtype) {
-        case LUMA_F32: pass1_octets<LUMA_F32>(d, c, o_lo, o_hi, am, av); break;
-        case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, o_lo, o_hi, am, av); break;
-        default: pass1_octets<LUMA_F16>(d, c, o_lo, o_hi, am, av); break;
+        case LUMA_F32: pass1_octets<LUMA_F32>(d, c, lut, o_lo, o_hi, am, av); break;
+        case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, lut, o_lo, o_hi, am, av); break;
+        default: pass1_octets<LUMA_F16>(d, c, lut, o_lo, o_hi, am, av); break;
       }
       am = __reduce_max_sync(0xffffffffu, am);
       av = __reduce_max_sync(0xffffffffu, av);
@@ -603,15 +892,15 @@ __global__ void __launch_bounds__(kThreads) luma_pass_kernel(const LumaStepArgs 
                         ((uintptr_t)d.u_m % 8 == 0) && ((uintptr_t)d.u_w % 8 == 0);
       if (d.param_dtype == LUMA_F32) {
         switch (d.grad_dtype) {
-          case LUMA_F32: pass2_pairs<LUMA_F32, LUMA_F32>(d, c, k0, k1, vec2, p_lo, p_hi); break;
-          case LUMA_BF16: pass2_pairs<LUMA_F32, LUMA_BF16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
-          default: pass2_pairs<LUMA_F32, LUMA_F16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
+          case LUMA_F32: pass2_pairs<LUMA_F32, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+          case LUMA_BF16: pass2_pairs<LUMA_F32, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+          default: pass2_pairs<LUMA_F32, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
         }
       } else {
         switch (d.grad_dtype) {
-          case LUMA_F32: pass2_pairs<LUMA_BF16, LUMA_F32>(d, c, k0, k1, vec2, p_lo, p_hi); break;
-          case LUMA_BF16: pass2_pairs<LUMA_BF16, LUMA_BF16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
-          default: pass2_pairs<LUMA_BF16, LUMA_F16>(d, c, k0, k1, vec2, p_lo, p_hi); break;
+          case LUMA_F32: pass2_pairs<LUMA_BF16, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+          case LUMA_BF16: pass2_pairs<LUMA_BF16, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+          default: pass2_pairs<LUMA_BF16, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
         }
       }
     }
@@ -663,10 +952,18 @@ int device_info(DeviceInfo** out) {
       return fail(LUMA_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                   dev, prop.major, prop.minor);
     }
+    e = cudaFuncSetAttribute(luma_pass_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kLutBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass1)");
+    e = cudaFuncSetAttribute(luma_pass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kLutBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2)");
     int b1 = 0, b2 = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, luma_pass_kernel<false>, kThreads, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, luma_pass_kernel<false>, kThreadsPass1,
+                                                      kLutBytes);
     if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass1)");
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, luma_pass_kernel<true>, kThreads, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, luma_pass_kernel<true>, kThreadsPass2,
+                                                      kLutBytes);
     if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass2)");
     di.sms = prop.multiProcessorCount;
     di.ctas_pass1 = di.sms * (b1 > 0 ? b1 : 1);
@@ -677,9 +974,9 @@ int device_info(DeviceInfo** out) {
   return LUMA_OK;
 }
 
-int grid_for(int64_t total_octets, int max_ctas) {
-  // at least one full tile (kThreads octets) per CTA
-  const int64_t want = (total_octets + kThreads - 1) / kThreads;
+int grid_for(int64_t total_octets, int threads, int max_ctas) {
+  // at least one full tile (one octet per thread) per CTA
+  const int64_t want = (total_octets + threads - 1) / threads;
   return (int)(want < max_ctas ? (want > 0 ? want : 1) : max_ctas);
 }
 
@@ -720,14 +1017,16 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[0]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  luma_pass_kernel<false><<<grid_for(a.total_octets, di->ctas_pass1), kThreads, 0, s>>>(a);
+  luma_pass_kernel<false><<<grid_for(a.total_octets, kThreadsPass1, di->ctas_pass1), kThreadsPass1,
+                            kLutBytes, s>>>(a, 1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 1");
   if (a.events[1]) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[1]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  luma_pass_kernel<true><<<grid_for(a.total_octets, di->ctas_pass2), kThreads, 0, s>>>(a);
+  luma_pass_kernel<true><<<grid_for(a.total_octets, kThreadsPass2, di->ctas_pass2), kThreadsPass2,
+                           kLutBytes, s>>>(a, 1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
   if (a.events[2]) {

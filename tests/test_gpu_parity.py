@@ -195,3 +195,54 @@ def test_export_decode_bit_exact():
         v = (1.0 / w - 1e-8).clamp(min=0).square()
         assert torch.equal(exp["state"][k]["exp_avg"], m)
         assert torch.equal(exp["state"][k]["exp_avg_sq"], v)
+
+
+def _crafted_grads(step, n, kind, gen):
+    """Gradients that stress the pass-1 maximum search (ties, near-ties,
+    zeros, subnormals, isolated spikes, sign flips)."""
+    base = torch.randn(n, generator=gen) * 1e-2
+    if kind == "const":
+        return torch.full((n,), 3e-3)
+    if kind == "ulp_ties":
+        c = torch.full((n,), 2.5e-3)
+        bits = c.view(torch.int32) + torch.arange(n, dtype=torch.int32) % 5
+        return bits.view(torch.float32)
+    if kind == "zeros":
+        return torch.zeros(n)
+    if kind == "subnormal":
+        return torch.randn(n, generator=gen) * 1e-41
+    if kind == "spike_last":
+        base[-1] = 7.0
+        return base
+    if kind == "spike_first":
+        base[0] = -7.0
+        return base
+    if kind == "flip":
+        return torch.full((n,), 1e-2 * (-1.0) ** step) + base * 1e-4
+    raise ValueError(kind)
+
+
+@pytest.mark.parametrize("beta1", [0.9, 0.0])
+def test_scale_max_adversarial_bit_exact(beta1):
+    LUMA = _luma()
+    kinds = ["const", "ulp_ties", "zeros", "subnormal", "spike_last", "spike_first", "flip"]
+    sizes = [4099, 70_003, 1_000_001]
+    gen = torch.Generator().manual_seed(3)
+    shapes = [(n,) for n in sizes for _ in kinds]
+    pk = [(torch.randn(s, generator=gen) * 0.02).to(DEV) for s in shapes]
+    po = [t.clone() for t in pk]
+    opt = LUMA(pk, lr=1e-3, betas=(beta1, 0.999))
+    orc = OracleLUMA(po, lr=1e-3, betas=(beta1, 0.999), draws=_philox_draws(opt))
+    for step in range(1, 5):
+        k = 0
+        for n in sizes:
+            for kind in kinds:
+                g = _crafted_grads(step, n, kind, gen).to(DEV)
+                pk[k].grad = g.clone()
+                po[k].grad = g.clone()
+                k += 1
+        opt.step()
+        orc.step()
+        for i, (a, b) in enumerate(zip(pk, po)):
+            assert torch.equal(a, b), f"step {step} tensor {i} ({kinds[i % len(kinds)]})"
+        _assert_same_state(f"step {step}", opt, orc, pk, po, [{"params": pk}])
