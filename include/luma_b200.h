@@ -174,6 +174,38 @@ typedef struct LumaStepArgs {
 int luma_step(const LumaStepArgs* args, void* stream);
 
 /*
+ * luma_step_noalloc — the same step as luma_step for callers that cannot
+ * allocate device memory of their own.  No counterpart in the reference.
+ *
+ * Who needs it: a host whose device memory is owned by another allocator
+ * (a framework arena or caching allocator that has reserved the free HBM, an
+ * FFI embedding with a fixed budget) or that must not call cudaMalloc from
+ * its step thread (cudaMalloc/cudaFree synchronise the device).  Such a
+ * caller still provides the tensors, the descriptor and row tables and the
+ * LumaSlot state, but pass 1's per-tensor accumulators (the amax_m, amax_v
+ * and done fields, which luma_step keeps in the caller's slots) come from a
+ * scratch array built into the library: LUMA_NOALLOC_MAX_DESCS entries of
+ * 16 bytes (64 KB), held by every GPU that loads the library until the
+ * process exits.  The slots' accumulator fields are not touched.
+ *
+ * Limits and behaviour:
+ *  - at most LUMA_NOALLOC_MAX_DESCS descriptors per call; larger tables are
+ *    rejected with LUMA_ERR_INVALID (use luma_step);
+ *  - the first call on a device looks up the scratch address on that device
+ *    (cudaGetSymbolAddress with the device current); make that first call
+ *    before any stream capture;
+ *  - each call clears the scratch entries it uses (cudaMemsetAsync on
+ *    `stream`), so a previous call's leftovers never leak into a new one;
+ *  - all calls share the one array: calls whose kernels can overlap on the
+ *    GPU (different streams without ordering) race and give wrong scales;
+ *    serialise them;
+ *  - nothing here allocates: no cudaMalloc, cudaFree or allocating library
+ *    routine is called.
+ */
+#define LUMA_NOALLOC_MAX_DESCS 4096
+int luma_step_noalloc(const LumaStepArgs* args, void* stream);
+
+/*
  * Decode codes to float32 AdamW moments (reference optimizer.py:231-235 /
  * functional.py:113-126): exp_avg[i] = sign(q_m) expm1(|q_m| dm),
  * w = w_min exp(q_w dw), exp_avg_sq[i] = max(1/w - eps32, 0)^2, with the

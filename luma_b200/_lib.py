@@ -77,8 +77,10 @@ class LumaStepArgs(ctypes.Structure):
 EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
                   SLOT_DTYPE.itemsize, ctypes.sizeof(LumaStepArgs))
 
-EXPORTED = ("luma_step", "luma_decode", "luma_abi_version", "luma_struct_sizes",
-            "luma_last_error")
+EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_abi_version",
+            "luma_struct_sizes", "luma_last_error")
+
+NOALLOC_MAX_DESCS = 4096  # LUMA_NOALLOC_MAX_DESCS
 
 _lib = None
 _lock = threading.Lock()
@@ -109,6 +111,8 @@ def lib() -> ctypes.CDLL:
         h.luma_last_error.argtypes = []
         h.luma_step.restype = ctypes.c_int
         h.luma_step.argtypes = [ctypes.POINTER(LumaStepArgs), ctypes.c_void_p]
+        h.luma_step_noalloc.restype = ctypes.c_int
+        h.luma_step_noalloc.argtypes = [ctypes.POINTER(LumaStepArgs), ctypes.c_void_p]
         h.luma_decode.restype = ctypes.c_int
         h.luma_decode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                   ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,

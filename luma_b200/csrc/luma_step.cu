@@ -59,6 +59,22 @@ constexpr int kLutEntries = 32769;
 constexpr int64_t kLutMinElems = 131072;
 constexpr size_t kLutBytes = kLutEntries * sizeof(float);
 
+// Pass-1 accumulators of one tensor (the amax_m / amax_v / done fields of a
+// LumaSlot) for luma_step_noalloc, which keeps them in the library's own
+// static device array instead of the caller's slots.
+struct PassAccum {
+  uint32_t amax_m;
+  uint32_t amax_v;
+  unsigned long long done;
+};
+static_assert(sizeof(PassAccum) == 16, "PassAccum layout");
+
+// Scratch of luma_step_noalloc: LUMA_NOALLOC_MAX_DESCS x 16 bytes, part of the
+// module image, so every GPU that loads the library holds it until exit.
+// Host code must not use this name as a device address; the set-up in
+// noalloc_scratch() fetches the address with cudaGetSymbolAddress.
+static __device__ __align__(256) PassAccum g_noalloc_accum[LUMA_NOALLOC_MAX_DESCS];
+
 // ---------------------------------------------------------------------------
 // Error reporting
 // ---------------------------------------------------------------------------
@@ -804,9 +820,11 @@ __device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShare
   if (pass2) s.enc = slot->grid[t & 1];
 }
 
-template <bool PASS2>
+// kStaticAcc: pass-1 accumulators at acc[descriptor index] (luma_step_noalloc)
+// instead of in the caller's LumaSlot (luma_step).
+template <bool PASS2, bool kStaticAcc = false>
 __global__ void __launch_bounds__(PASS2 ? kThreadsPass2 : kThreadsPass1, 1)
-luma_pass_kernel(const LumaStepArgs a, const int lut_ok) {
+luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
   constexpr int kThreads = PASS2 ? kThreadsPass2 : kThreadsPass1;
   constexpr int kWarps = kThreads / 32;
   __shared__ SegShared s;
@@ -856,16 +874,20 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok) {
       if (threadIdx.x == 0) {
         for (int w = 1; w < kWarps; ++w) { am = max(am, red_m[w]); av = max(av, red_v[w]); }
         LumaSlot* slot = a.slots + d.slot;
-        atomicMax(&slot->amax_m, am);
-        atomicMax(&slot->amax_v, av);
+        uint32_t* amax_m = kStaticAcc ? &acc[di].amax_m : &slot->amax_m;
+        uint32_t* amax_v = kStaticAcc ? &acc[di].amax_v : &slot->amax_v;
+        unsigned long long* done =
+            kStaticAcc ? &acc[di].done : reinterpret_cast<unsigned long long*>(&slot->done);
+        atomicMax(amax_m, am);
+        atomicMax(amax_v, av);
         __threadfence();
         const unsigned long long mine = (unsigned long long)(o_hi - o_lo);
-        const unsigned long long prev = atomicAdd((unsigned long long*)&slot->done, mine);
+        const unsigned long long prev = atomicAdd(done, mine);
         if (prev + mine == (unsigned long long)n_oct) {
           // Last contributor for this tensor: every other CTA's maxima are in.
           __threadfence();
-          const uint32_t bm = atomicOr(&slot->amax_m, 0u);
-          const uint32_t bv = atomicOr(&slot->amax_v, 0u);
+          const uint32_t bm = atomicOr(amax_m, 0u);
+          const uint32_t bv = atomicOr(amax_v, 0u);
           const double smt = (double)__uint_as_float(bm);
           const double svt = (double)__uint_as_float(bv);
           // S_m = max(S_m_t, 1e-9); S_v = max(S_v_t, 0.0) with Python's max()
@@ -873,9 +895,9 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok) {
           const double S_m = (LUMA_SCALE_FLOOR_M > smt) ? LUMA_SCALE_FLOOR_M : smt;
           const double S_v = (0.0 > svt) ? 0.0 : svt;
           make_grid(S_m, S_v, s.row.eps, &slot->grid[s.row.step & 1]);
-          slot->amax_m = 0u;
-          slot->amax_v = 0u;
-          slot->done = 0ull;
+          *amax_m = 0u;
+          *amax_v = 0u;
+          *done = 0ull;
         }
       }
     } else {
@@ -931,6 +953,7 @@ struct DeviceInfo {
   int sms = 0;
   int ctas_pass1 = 0;
   int ctas_pass2 = 0;
+  PassAccum* noalloc_acc = nullptr;  // device address of g_noalloc_accum
 };
 
 constexpr int kMaxDevices = 64;
@@ -958,6 +981,12 @@ int device_info(DeviceInfo** out) {
     e = cudaFuncSetAttribute(luma_pass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kLutBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2)");
+    e = cudaFuncSetAttribute(luma_pass_kernel<false, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLutBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass1 noalloc)");
+    e = cudaFuncSetAttribute(luma_pass_kernel<true, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLutBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2 noalloc)");
     int b1 = 0, b2 = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, luma_pass_kernel<false>, kThreadsPass1,
                                                       kLutBytes);
@@ -978,6 +1007,20 @@ int grid_for(int64_t total_octets, int threads, int max_ctas) {
   // at least one full tile (one octet per thread) per CTA
   const int64_t want = (total_octets + threads - 1) / threads;
   return (int)(want < max_ctas ? (want > 0 ? want : 1) : max_ctas);
+}
+
+// Address of g_noalloc_accum on the current device, fetched once per device
+// (with that device current) on the first luma_step_noalloc call there.
+int noalloc_scratch(DeviceInfo* di, PassAccum** out) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (di->noalloc_acc == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_accum);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+    di->noalloc_acc = static_cast<PassAccum*>(ptr);
+  }
+  *out = di->noalloc_acc;
+  return LUMA_OK;
 }
 
 }  // namespace
@@ -1018,7 +1061,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
   luma_pass_kernel<false><<<grid_for(a.total_octets, kThreadsPass1, di->ctas_pass1), kThreadsPass1,
-                            kLutBytes, s>>>(a, 1);
+                            kLutBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 1");
   if (a.events[1]) {
@@ -1026,7 +1069,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
   luma_pass_kernel<true><<<grid_for(a.total_octets, kThreadsPass2, di->ctas_pass2), kThreadsPass2,
-                           kLutBytes, s>>>(a, 1);
+                           kLutBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
   if (a.events[2]) {
@@ -1052,6 +1095,58 @@ int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel, float dm,
       q_m, q_w, numel, dm, w_min, dw, eps32, exp_avg, exp_avg_sq);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch decode");
+  return LUMA_OK;
+}
+
+
+int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
+  g_err[0] = '\0';
+  if (args == nullptr) return fail(LUMA_ERR_INVALID, "luma_step_noalloc: args is NULL");
+  const LumaStepArgs a = *args;
+  if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0)
+    return fail(LUMA_ERR_INVALID,
+                "luma_step_noalloc: negative size (n_desc=%d n_rows=%d total_octets=%lld)",
+                a.n_desc, a.n_rows, (long long)a.total_octets);
+  if (a.n_desc > LUMA_NOALLOC_MAX_DESCS)
+    return fail(LUMA_ERR_INVALID,
+                "luma_step_noalloc: %d tensors exceed the built-in scratch of %d; use luma_step "
+                "with caller-provided slots for larger tables",
+                a.n_desc, LUMA_NOALLOC_MAX_DESCS);
+  if (a.n_desc == 0 || a.total_octets == 0) return LUMA_OK;
+  if (a.descs == nullptr || a.slots == nullptr || a.rows == nullptr || a.n_rows == 0)
+    return fail(LUMA_ERR_INVALID,
+                "luma_step_noalloc: descs/slots/rows must be non-NULL and n_rows > 0");
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st != LUMA_OK) return st;
+  PassAccum* acc = nullptr;
+  st = noalloc_scratch(di, &acc);
+  if (st != LUMA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents; the accumulators must start
+  // at zero (a completed call leaves them zero, an aborted one may not).
+  cudaError_t e = cudaMemsetAsync(acc, 0, sizeof(PassAccum) * (size_t)a.n_desc, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(noalloc scratch)");
+  if (a.events[0]) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[0]), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  luma_pass_kernel<false, true><<<grid_for(a.total_octets, kThreadsPass1, di->ctas_pass1),
+                                  kThreadsPass1, kLutBytes, s>>>(a, 1, acc);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch pass 1 (noalloc)");
+  if (a.events[1]) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[1]), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  luma_pass_kernel<true, true><<<grid_for(a.total_octets, kThreadsPass2, di->ctas_pass2),
+                                 kThreadsPass2, kLutBytes, s>>>(a, 1, acc);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch pass 2 (noalloc)");
+  if (a.events[2]) {
+    e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[2]), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
   return LUMA_OK;
 }
 
