@@ -339,6 +339,97 @@ def run_luma(args, rank, world, local_rank):
     }
 
 
+def run_zero(args, rank, world, local_rank):
+    """ZeRO-1: this rank steps its flat shard of the whole model, then the
+    bf16 params are all-gathered in place over NCCL (strong scaling)."""
+    import torch.distributed as dist
+
+    from luma_b200.zero import ZeroLUMA, plan_layout
+
+    device = torch.device("cuda", local_rank)
+    cfg = CONFIGS[args.config]
+    shapes = cfg["shapes"]()
+    numels = [numel(s) for s in shapes]
+    n_params = sum(numels)
+    lay = plan_layout(numels, world)
+    gen = torch.Generator(device=device).manual_seed(0)
+    flat = torch.empty(lay.total, dtype=cfg["pdt"], device=device)
+    flat.normal_(0.0, 0.02, generator=gen)
+    gshard = torch.empty(lay.shard, dtype=cfg["gdt"], device=device)
+    gshard.normal_(0.0, cfg["gscale"], generator=gen)
+    opt = ZeroLUMA(flat, lay, rank, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                   base_seed=1234)
+    for _ in range(max(args.warmup, 1)):
+        opt.step(gshard)
+    torch.cuda.synchronize()
+    K = args.steps
+    stream = torch.cuda.current_stream()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    for quad in evs:
+        for e in quad:
+            e.record(stream)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank)
+    dist.barrier()
+    torch.cuda.synchronize()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    start.record(stream)
+    for k in range(K):
+        opt.events = tuple(e.cuda_event for e in evs[k][:3])
+        opt.step_local(gshard)
+        opt.gather()
+        evs[k][3].record(stream)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    opt.events = None
+    clocks = sampler.stop() if rank == 0 else None
+    dist.barrier()
+    total_ms = start.elapsed_time(stop)
+    p1 = statistics.mean(evs[k][0].elapsed_time(evs[k][1]) for k in range(K))
+    p2 = statistics.mean(evs[k][1].elapsed_time(evs[k][2]) for k in range(K))
+    ag = statistics.mean(evs[k][2].elapsed_time(evs[k][3]) for k in range(K))
+    t = torch.tensor([total_ms, p1, p2, ag], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, p1, p2, ag = (float(x) for x in t.tolist())
+
+    e2e = None
+    if not args.no_e2e:
+        host = torch.empty(gshard.shape, dtype=gshard.dtype, pin_memory=True)
+        host.copy_(gshard)
+        E = max(2, min(K, 5))
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(E):
+            gshard.copy_(host, non_blocking=True)
+            opt.step(gshard)
+            opt.engine.read_slots()
+        el = torch.tensor([time.perf_counter() - t0], device=device)
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(n_params * E / float(el.item()) / 1e9, 3), "unit": "Gparams/s",
+               "h2d_bytes_per_step": host.numel() * host.element_size(),
+               "d2h_bytes_per_step": opt.engine.slots.numel(), "steps": E}
+
+    p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
+    peak, peak_kind = measured_peak()
+    achieved = lay.shard * p2b / (p2 * 1e-3) / 1e9
+    gather_bytes = (world - 1) * lay.shard * flat.element_size()
+    return {
+        "n_params": n_params, "ms_per_step": total_ms / K, "pass1_ms": p1, "pass2_ms": p2,
+        "allgather_ms": ag, "allgather_gbs_per_rank": round(gather_bytes / (ag * 1e-3) / 1e9, 1),
+        "step_only_gparams": round(n_params / ((p1 + p2) * 1e-3) / 1e9, 3),
+        "shard_params": lay.shard, "bytes_per_param": p1b + p2b, "pass2_bytes_per_param": p2b,
+        "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<pass2>",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": None},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": 2 * K,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -377,17 +468,25 @@ def main():
         return
 
     if world > 1:
-        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    res = run_luma(args, rank, world, local_rank)
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                             timeout=datetime.timedelta(seconds=300))
+        res = run_zero(args, rank, world, local_rank)
+        config_out["parallelism"] = f"zero1-dp{world} (flat shards, per-shard scales, NCCL bf16 all-gather)"
+        scaling = "strong"
+    else:
+        res = run_luma(args, rank, world, local_rank)
+        scaling = "weak"
     if rank == 0:
-        n = res["n_params"] * world
+        n = res["n_params"]
         ms = res["ms_per_step"]
         value = n / (ms * 1e-3) / 1e9
-        hbm = res["n_params"] * res["bytes_per_param"] / (ms * 1e-3) / 1e9
+        hbm = n / world * res["bytes_per_param"] / ((res["pass1_ms"] + res["pass2_ms"]) * 1e-3) / 1e9
         peak, peak_kind = measured_peak()
         line = {"metric": METRIC, "value": round(value, 3), "unit": "Gparams/s",
                 "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 1),
-                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": scaling,
                 "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config_out,
                 "hbm_gbs_per_gpu": round(hbm, 1),
                 "hbm_frac_of_measured_peak": round(hbm / peak, 4),
@@ -395,6 +494,9 @@ def main():
                 "pass1_ms": round(res["pass1_ms"], 4), "pass2_ms": round(res["pass2_ms"], 4),
                 "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
                 "gpu_launches": res["gpu_launches"]}
+        for key in ("allgather_ms", "allgather_gbs_per_rank", "step_only_gparams", "shard_params"):
+            if key in res:
+                line[key] = res[key]
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.config, 10, 2)
         print(json.dumps(line))

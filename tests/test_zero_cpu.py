@@ -1,0 +1,101 @@
+"""ZeRO-1 shard planning and the post-step gather, on CPU.
+
+The planner must cut the flat parameter space into equal shards whose
+per-tensor segments cover every element exactly once, start 8-aligned inside
+their tensor (Philox counter and 128-bit loads) and keep the global tensor
+index; the gather is checked with two gloo ranks on CPU: each rank writes its
+shard, the in-place all_gather_into_tensor must rebuild the full buffer."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from luma_b200.zero import ALIGN, flat_views, plan_layout, shard_segments
+
+
+def llama_like_numels():
+    d, kv, ffn = 512, 128, 1792
+    out = [5000 * d]
+    for _ in range(3):
+        out += [d * d, kv * d, kv * d, d * d, ffn * d, ffn * d, d * ffn, d, d]
+    return out + [d, 5000 * d]
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("numels", [llama_like_numels(), [1, 7, 8, 9, 1025, 3, 0, 17],
+                                    list(np.random.default_rng(0).integers(1, 5000, 300))])
+def test_segments_partition_every_tensor(world, numels):
+    lay = plan_layout(numels, world)
+    assert lay.shard % ALIGN == 0 and lay.total >= sum(-(-n // ALIGN) * ALIGN for n in numels)
+    assert all(s % ALIGN == 0 for s in lay.starts)
+    covered = [np.zeros(n, dtype=np.int32) for n in numels]
+    for r in range(world):
+        for sg in shard_segments(lay, r):
+            assert r * lay.shard <= sg.flat and sg.flat + sg.length <= (r + 1) * lay.shard
+            assert sg.offset % ALIGN == 0 and sg.flat % ALIGN == 0
+            assert sg.flat == lay.starts[sg.tensor] + sg.offset
+            covered[sg.tensor][sg.offset:sg.offset + sg.length] += 1
+    for c in covered:
+        assert np.all(c == 1)
+
+
+def test_flat_views_share_storage():
+    shapes = [(3, 5), (7,), (2, 2, 2)]
+    lay = plan_layout([15, 7, 8], 2)
+    flat = torch.zeros(lay.total)
+    views = flat_views(flat, lay, shapes)
+    for k, v in enumerate(views):
+        v.fill_(k + 1)
+    for k, (v, s) in enumerate(zip(views, lay.starts)):
+        assert v.data_ptr() == flat.data_ptr() + 4 * s
+        assert torch.all(flat[s:s + v.numel()] == k + 1)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gather_worker(rank, world, port, numels, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lay = plan_layout(numels, world)
+        flat = torch.full((lay.total,), -1.0)
+        # "step": this rank writes a known value into every element it owns
+        for sg in shard_segments(lay, rank):
+            flat[sg.flat:sg.flat + sg.length] = torch.arange(sg.length, dtype=torch.float32) + \
+                1000.0 * sg.tensor + sg.offset
+        shard = flat[rank * lay.shard:(rank + 1) * lay.shard].clone()
+        out = torch.empty_like(flat)
+        dist.all_gather_into_tensor(out, shard)
+        ok = True
+        for t, (n, s) in enumerate(zip(lay.numels, lay.starts)):
+            want = torch.arange(n, dtype=torch.float32) + 1000.0 * t
+            ok &= bool(torch.equal(out[s:s + n], want))
+        out_q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_gather_rebuilds_params_gloo(world):
+    numels = [37, 1024, 5, 999, 64]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, numels, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert all(results.values()), results
