@@ -73,6 +73,11 @@ def ragged_shapes(n=10_000, seed=0):
     return [(max(1, int(round(2 ** rng.uniform(0, 20)))),) for _ in range(n)]
 
 
+def llama_layer_shapes():
+    d, kv, ffn = 4096, 1024, 14336
+    return [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
+
+
 def cpu21m_shapes():
     return [(1024, 1024)] * 4 + [(4096, 1024)] * 2 + [(1024, 4096)] * 2
 
@@ -80,6 +85,9 @@ def cpu21m_shapes():
 CONFIGS = {
     "llama8b": dict(shapes=llama3_8b_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
                     gscale=1e-3, name="Llama-3-8B shapes (291 tensors), bf16 params, bf16 grads"),
+    "llama_layer": dict(shapes=llama_layer_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
+                        gscale=1e-3, name="one Llama-3-8B decoder layer (9 tensors, 218,112,000 "
+                        "params), bf16 params, bf16 grads (profiling case)"),
     "gpt2": dict(shapes=gpt2_small_shapes, pdt=torch.float32, gdt=torch.bfloat16,
                  gscale=1e-3, name="GPT-2 small shapes (148 tensors), fp32 params, bf16 grads"),
     "ragged": dict(shapes=ragged_shapes, pdt=torch.float32, gdt=torch.float32,
@@ -450,7 +458,7 @@ def main():
         str(cfg["gdt"]).replace("torch.", "") + ", codes int16"
     config_out = {"workload": cfg["name"], "bytes_per_param": p1b + p2b,
                   "l2": "inputs larger than L2 (resident params+grads+codes >> 126 MB)"
-                  if args.config in ("llama8b", "ragged") else "working set may fit L2",
+                  if args.config in ("llama8b", "ragged", "llama_layer") else "working set may fit L2",
                   "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single"}
 
     if args.impl == "reference":

@@ -47,8 +47,8 @@ static_assert(sizeof(LumaSlot) == 144, "LumaSlot layout");
 namespace {
 
 constexpr int kThreads = 256;           // luma_decode
-constexpr int kThreadsPass1 = 512;      // one CTA per SM (128 KB decode table)
-constexpr int kThreadsPass2 = 512;      // one CTA per SM, <= 128 registers
+constexpr int kThreadsPass1 = 1024;     // one CTA per SM (128 KB decode table)
+constexpr int kThreadsPass2 = 640;      // one CTA per SM, <= 96 registers (measured best)
 constexpr int kMaxWarps = 32;
 
 // Decode table of expm1f(fl(|q| * delta_m)) for |q| = 0..32768, built in
@@ -173,8 +173,9 @@ struct Consts {
   float n_sm32, n_dm, n_inv_dm, n_inv_zm, n_wmin, n_inv_wmin, n_dw, n_inv_dw, n_inv_zw;
   int n_dw_pos;
   int init;
-  // LogSR decision filter usable (delta small enough for the series)
-  bool series_m, series_w;
+  // LogSR decision margins: kDecisionMargin where the series is valid,
+  // 2 (always take the exact path) where delta is too large for it
+  float margin_m, margin_w;
   // pass-1 approximate decode
   float o_dw_log2e;
   float tau_v;  // kBoundEps * eps^2
@@ -225,20 +226,25 @@ __device__ __forceinline__ float adamw(const Consts& c, float p, float mn, float
 // LogSR decision  u < p*,  p* = fl(expm1f(fl(frac * delta)) * inv_z)
 // (functional.py:64-66).  For delta <= kSeriesMaxDelta the series
 // x + x^2/2 + x^3/6 (x = fl(frac * delta) <= delta) is within 3e-7 of p*:
-// expm1f is within 1 ulp, the omitted x^4/24 term is below 2e-9 relative,
-// and the roundings add under 2 ulp.  Only when u falls within kDecisionMargin
-// (6x that bound) of the series value is expm1f evaluated, so the decision,
-// and therefore the code, is the one the exact expression gives.
-constexpr float kSeriesMaxDelta = 0.01f;
+// expm1f is within 1 ulp, the omitted x^4/24 term is below 6e-8 relative,
+// and the roundings add under 2 ulp.  Only when u falls within the margin
+// (kDecisionMargin, 6x that bound) of the series value is expm1f evaluated,
+// so the decision, and therefore the code, is the one the exact expression
+// gives.  Any finite float64 grid has delta_m <= 0.0028 and delta_w <= 0.0109;
+// beyond kSeriesMaxDelta the margin is 2, which sends every element to the
+// exact expression.
+constexpr float kSeriesMaxDelta = 0.011f;
 constexpr float kDecisionMargin = 0x1.0p-19f;
 
-__device__ __forceinline__ bool logsr_up(float fr, float delta, float inv_z, float u, bool series) {
+__device__ __forceinline__ float decision_margin(float delta) {
+  return delta <= kSeriesMaxDelta ? kDecisionMargin : 2.0f;
+}
+
+__device__ __forceinline__ bool logsr_up(float fr, float delta, float inv_z, float u, float margin) {
   const float x = __fmul_rn(fr, delta);
-  if (series) {
-    const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
-    const float diff = __fsub_rn(u, __fmul_rn(e, inv_z));
-    if (fabsf(diff) > kDecisionMargin) return diff < 0.0f;
-  }
+  const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
+  const float diff = __fsub_rn(u, __fmul_rn(e, inv_z));
+  if (fabsf(diff) > margin) return diff < 0.0f;
   return u < __fmul_rn(expm1f(x), inv_z);
 }
 
@@ -248,7 +254,7 @@ __device__ __forceinline__ int quant_m(const Consts& c, float mn, float u) {
   const float y = __fmul_rn(log1pf(fabsf(mc)), c.n_inv_dm);
   const float fy = floorf(y);
   const float fr = __fsub_rn(y, fy);
-  float r = __fadd_rn(fy, logsr_up(fr, c.n_dm, c.n_inv_zm, u, c.series_m) ? 1.0f : 0.0f);
+  float r = __fadd_rn(fy, logsr_up(fr, c.n_dm, c.n_inv_zm, u, c.margin_m) ? 1.0f : 0.0f);
   r = clamp_keepnan(r, 0.0f, (float)LUMA_K_M);
   const float sg = (mc > 0.0f) ? 1.0f : ((mc < 0.0f) ? -1.0f : 0.0f);
   return (int)__fmul_rn(sg, r);
@@ -256,13 +262,14 @@ __device__ __forceinline__ int quant_m(const Consts& c, float mn, float u) {
 
 // _quantize_preconditioner (functional.py:153-176) with _log_sr.
 __device__ __forceinline__ uint32_t quant_w(const Consts& c, float vn, float u) {
-  if (!c.n_dw_pos) return 0u;  // delta_w == 0: y = 0 and _log_sr returns 0
+  // delta_w == 0 (_log_sr returns 0): inv_dw = 0 makes y = 0, frac = 0 and
+  // p* = 0, so the expression below yields 0 without a branch.
   const float den = __fadd_rn(__fsqrt_rn(clamp_min_keepnan(vn, 0.0f)), c.eps32);
   const float w = clamp_keepnan(__frcp_rn(den), c.n_wmin, c.w_max);
   const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
   const float fy = floorf(y);
   const float fr = __fsub_rn(y, fy);
-  float r = __fadd_rn(fy, logsr_up(fr, c.n_dw, c.n_inv_zw, u, c.series_w) ? 1.0f : 0.0f);
+  float r = __fadd_rn(fy, logsr_up(fr, c.n_dw, c.n_inv_zw, u, c.margin_w) ? 1.0f : 0.0f);
   r = clamp_keepnan(r, 0.0f, (float)LUMA_K_W);
   return (uint32_t)(int)r;  // .to(int32) then two's-complement wrap to int16
 }
@@ -769,6 +776,25 @@ __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Const
 // Kernels
 // ---------------------------------------------------------------------------
 
+// Segment-level selection of the pass-2 loop for the tensor's dtypes.
+__device__ __forceinline__ void dispatch_pass2(const LumaTensorDesc& d, const Consts& c,
+                                               const float* lut, uint32_t k0, uint32_t k1,
+                                               bool vec2, int64_t p_lo, int64_t p_hi) {
+  if (d.param_dtype == LUMA_F32) {
+    switch (d.grad_dtype) {
+      case LUMA_F32: pass2_pairs<LUMA_F32, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_pairs<LUMA_F32, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_pairs<LUMA_F32, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+    }
+  } else {
+    switch (d.grad_dtype) {
+      case LUMA_F32: pass2_pairs<LUMA_BF16, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_pairs<LUMA_BF16, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_pairs<LUMA_BF16, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+    }
+  }
+}
+
 struct SegShared {
   LumaTensorDesc d;
   LumaStepRow row;
@@ -797,8 +823,8 @@ __device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Cons
     c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
     c.n_wmin = s.enc.w_min; c.n_inv_wmin = s.enc.inv_wmin; c.n_dw = s.enc.dw;
     c.n_inv_dw = s.enc.inv_dw; c.n_inv_zw = s.enc.inv_zw; c.n_dw_pos = s.enc.dw_pos;
-    c.series_m = c.n_dm <= kSeriesMaxDelta;
-    c.series_w = c.n_dw <= kSeriesMaxDelta;
+    c.margin_m = decision_margin(c.n_dm);
+    c.margin_w = decision_margin(c.n_dw);
   } else {
     c.o_dw_log2e = c.o_dw * 1.44269504f;
     c.tau_v = kBoundEps * c.eps32 * c.eps32 + kTinyAbs;
@@ -912,19 +938,7 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
       const bool vec2 = ((uintptr_t)d.param % pes == 0) && ((uintptr_t)d.grad % ges == 0) &&
                         ((uintptr_t)d.q_m % 4 == 0) && ((uintptr_t)d.q_w % 4 == 0) &&
                         ((uintptr_t)d.u_m % 8 == 0) && ((uintptr_t)d.u_w % 8 == 0);
-      if (d.param_dtype == LUMA_F32) {
-        switch (d.grad_dtype) {
-          case LUMA_F32: pass2_pairs<LUMA_F32, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-          case LUMA_BF16: pass2_pairs<LUMA_F32, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-          default: pass2_pairs<LUMA_F32, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-        }
-      } else {
-        switch (d.grad_dtype) {
-          case LUMA_F32: pass2_pairs<LUMA_BF16, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-          case LUMA_BF16: pass2_pairs<LUMA_BF16, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-          default: pass2_pairs<LUMA_BF16, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-        }
-      }
+      dispatch_pass2(d, c, lut, k0, k1, vec2, p_lo, p_hi);
     }
     __syncthreads();  // s is rewritten for the next tensor
     pos = d.oct_begin + o_hi;
