@@ -216,6 +216,21 @@ int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel,
                 float dm, float w_min, float dw, float eps32,
                 float* exp_avg, float* exp_avg_sq, void* stream);
 
+/*
+ * Quantize float32 AdamW moments into codes on `grid` (host pointer; built
+ * for (S_m, S_v, eps) with S_m = max(max|m|, 1e-9), S_v = max(max v, 0)):
+ * q_m from m, q_w from v (v >= 0), LogSR with the Philox stream keyed by
+ * `seed` and counter offset `rng_offset` (even), or with the injected
+ * uniforms u_m/u_w when both are non-NULL.  eps32 = fl32(eps), w_max =
+ * fl32(1/eps).
+ * Reference: optimizer.py:256-335 import_adamw_state, quantizer calls at
+ * optimizer.py:315-321 (functional.py:133-176), seed (base_seed, step 0, idx).
+ */
+int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid* grid,
+                  float eps32, float w_max, int64_t seed, int64_t rng_offset,
+                  const float* u_m, const float* u_w, int16_t* q_m, int16_t* q_w,
+                  void* stream);
+
 /* ABI version (LUMA_ABI_VERSION). */
 int luma_abi_version(void);
 

@@ -77,8 +77,8 @@ class LumaStepArgs(ctypes.Structure):
 EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
                   SLOT_DTYPE.itemsize, ctypes.sizeof(LumaStepArgs))
 
-EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_abi_version",
-            "luma_struct_sizes", "luma_last_error")
+EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_quantize",
+            "luma_abi_version", "luma_struct_sizes", "luma_last_error")
 
 NOALLOC_MAX_DESCS = 4096  # LUMA_NOALLOC_MAX_DESCS
 
@@ -117,6 +117,12 @@ def lib() -> ctypes.CDLL:
         h.luma_decode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                   ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        h.luma_quantize.restype = ctypes.c_int
+        h.luma_quantize.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                    ctypes.c_void_p, ctypes.c_float, ctypes.c_float,
+                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p]
         v = h.luma_abi_version()
         if v != ABI_VERSION:
             raise ImportError(f"libluma_b200 ABI {v}, expected {ABI_VERSION}")

@@ -957,6 +957,37 @@ __global__ void __launch_bounds__(kThreads) luma_decode_kernel(
   }
 }
 
+// Quantize float32 moments onto a grid (reference optimizer.py:315-321,
+// functional.py:133-176): Q_m from m, Q_w from v, uniforms from the Philox
+// stream keyed by `seed` (or injected).
+__global__ void __launch_bounds__(kThreads) luma_quantize_kernel(
+    const float* __restrict__ m, const float* __restrict__ v, int64_t n, const Consts c,
+    uint32_t k0, uint32_t k1, uint64_t ctr0, const float* __restrict__ u_m,
+    const float* __restrict__ u_w, int16_t* __restrict__ q_m, int16_t* __restrict__ q_w) {
+  const int64_t n_pairs = (n + 1) / 2;
+  for (int64_t P = (int64_t)blockIdx.x * kThreads + threadIdx.x; P < n_pairs;
+       P += (int64_t)gridDim.x * kThreads) {
+    float um[2], uw[2];
+    if (u_m != nullptr) {
+      um[0] = u_m[2 * P]; uw[0] = u_w[2 * P];
+      um[1] = (2 * P + 1 < n) ? u_m[2 * P + 1] : 0.0f;
+      uw[1] = (2 * P + 1 < n) ? u_w[2 * P + 1] : 0.0f;
+    } else {
+      const uint64_t ctr = ctr0 + (uint64_t)P;
+      const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+      um[0] = u24(r.x); uw[0] = u24(r.y); um[1] = u24(r.z); uw[1] = u24(r.w);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t e = 2 * P + h;
+      if (e < n) {
+        q_m[e] = (int16_t)quant_m(c, m[e], um[h]);
+        q_w[e] = (int16_t)(uint16_t)quant_w(c, v[e], uw[h]);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -1112,6 +1143,42 @@ int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel, float dm,
   return LUMA_OK;
 }
 
+
+int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid* grid,
+                  float eps32, float w_max, int64_t seed, int64_t rng_offset, const float* u_m,
+                  const float* u_w, int16_t* q_m, int16_t* q_w, void* stream) {
+  g_err[0] = '\0';
+  if (numel < 0) return fail(LUMA_ERR_INVALID, "luma_quantize: negative numel");
+  if (numel == 0) return LUMA_OK;
+  if (!m || !v || !grid || !q_m || !q_w)
+    return fail(LUMA_ERR_INVALID, "luma_quantize: NULL pointer");
+  if ((u_m == nullptr) != (u_w == nullptr))
+    return fail(LUMA_ERR_INVALID, "luma_quantize: u_m and u_w must both be set or both NULL");
+  if (rng_offset < 0 || (rng_offset & 1))
+    return fail(LUMA_ERR_INVALID, "luma_quantize: rng_offset must be even and >= 0");
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st != LUMA_OK) return st;
+  Consts c;
+  memset(&c, 0, sizeof(c));
+  const LumaGrid& gr = *grid;
+  c.eps32 = eps32; c.w_max = w_max;
+  c.n_sm32 = gr.s_m32; c.n_dm = gr.dm; c.n_inv_dm = gr.inv_dm; c.n_inv_zm = gr.inv_zm;
+  c.n_wmin = gr.w_min; c.n_inv_wmin = gr.inv_wmin; c.n_dw = gr.dw; c.n_inv_dw = gr.inv_dw;
+  c.n_inv_zw = gr.inv_zw; c.n_dw_pos = gr.dw_pos;
+  c.margin_m = gr.dm <= kSeriesMaxDelta ? kDecisionMargin : 2.0f;
+  c.margin_w = gr.dw <= kSeriesMaxDelta ? kDecisionMargin : 2.0f;
+  const uint64_t sd = (uint64_t)seed;
+  const int64_t n_pairs = (numel + 1) / 2;
+  const int64_t want = (n_pairs + kThreads - 1) / kThreads;
+  const int blocks = (int)(want < di->sms * 8 ? want : di->sms * 8);
+  luma_quantize_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      m, v, numel, c, (uint32_t)sd, (uint32_t)(sd >> 32), (uint64_t)rng_offset >> 1, u_m, u_w,
+      q_m, q_w);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch quantize");
+  return LUMA_OK;
+}
 
 int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
   g_err[0] = '\0';

@@ -180,7 +180,9 @@ class LUMA(Optimizer):
             st = self.state[p]
             param = self._unwrap_tensor(p)
             for key, v in cd.items():
-                st[key] = v.to(device=param.device).to(torch.int16)
+                # always a copy: a state dict taken from a live optimizer holds
+                # that optimizer's own code tensors
+                st[key] = v.to(device=param.device, dtype=torch.int16, copy=True)
         for p in params:
             st = self.state.get(p)
             if not st or "S_m" not in st:
@@ -241,6 +243,73 @@ class LUMA(Optimizer):
             pg["params"] = [param_to_idx[id(p)] for p in group["params"]]
             param_groups.append(pg)
         return {"state": adamw_state, "param_groups": param_groups}
+
+    def import_adamw_state(self, adamw_sd: dict) -> None:
+        """Quantize a ``torch.optim.AdamW`` state dict into LUMA codes.
+
+        Follows optimizer.py:256-335: per entry, step is kept, ``exp_avg`` and
+        ``exp_avg_sq`` (clamped at 0) become float32 on the param's device,
+        ``S_m = max(max|m|, 1e-9)``, ``S_v = max(max v, 0)``, and the codes are
+        written with LogSR on that grid, the uniforms keyed by the seed
+        ``(_base_seed, step 0, param index)`` (here the Philox stream).
+        Hyper-parameters are not imported.
+        """
+        all_params = []
+        group_of = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                group_of[len(all_params)] = group
+                all_params.append(p)
+        for idx_key, st_in in adamw_sd["state"].items():
+            idx = int(idx_key) if isinstance(idx_key, str) else idx_key
+            if idx >= len(all_params):
+                raise ValueError(f"AdamW state has index {idx} but LUMA only has "
+                                 f"{len(all_params)} parameters")
+            p = all_params[idx]
+            eps = group_of[idx]["eps"]
+            step_val = st_in["step"]
+            step = int(step_val.item() if isinstance(step_val, torch.Tensor) else step_val)
+            param = self._unwrap_tensor(p)
+            device = param.device if param is not None else p.device
+            if device.type != "cuda":
+                raise RuntimeError(f"LUMA backend 'cuda' requires CUDA tensors (param on {device}).")
+            m = st_in["exp_avg"].to(device).float().contiguous()
+            v = st_in["exp_avg_sq"].to(device).float().clamp(min=0.0).contiguous()
+            S_m = max(m.abs().max().item(), SCALE_FLOOR_M)
+            S_v = max(v.max().item(), 0.0)
+            grid = np.zeros(1, dtype=_lib.GRID_DTYPE)
+            grid[0] = grid_record(S_m, S_v, eps)
+            q_m = torch.empty(m.shape, dtype=torch.int16, device=device)
+            q_w = torch.empty(m.shape, dtype=torch.int16, device=device)
+            seed = ((0 << 32) | (idx * 2)) ^ self._base_seed  # functional.py:99-106, step 0
+            seed = ctypes.c_int64(seed & 0xFFFFFFFFFFFFFFFF).value
+            um = uw = None
+            if self._draw_hook is not None:
+                um, uw = (t.reshape(-1).contiguous() for t in self._draw_hook(idx, 0, m))
+            stream = torch.cuda.current_stream(device)
+            with torch.cuda.device(device):
+                _lib.check(_lib.lib().luma_quantize(
+                    m.data_ptr(), v.data_ptr(), m.numel(), grid.ctypes.data,
+                    float(np.float32(eps)), float(np.float32(1.0 / eps)), seed, 0,
+                    None if um is None else um.data_ptr(), None if uw is None else uw.data_ptr(),
+                    q_m.data_ptr(), q_w.data_ptr(), ctypes.c_void_p(stream.cuda_stream)),
+                    "luma_quantize")
+            state = self.state[p]
+            state["step"] = step
+            state["param_id"] = idx
+            state["Q_m"] = q_m
+            state["Q_w"] = q_w
+            slot = state.get("_slot")
+            if slot is None:
+                slot = self._new_slot(device)
+                state["_slot"] = slot
+            eng = self._engine(device)
+            eng.reset_slot(slot)
+            eng.write_grid(slot, step & 1, grid[0])
+            state.pop("S_m", None)
+            state.pop("S_v", None)
+            if um is not None:
+                torch.cuda.current_stream(device).synchronize()  # injected draws outlive the kernel
 
     # ------------------------------------------------------------------
     # step (optimizer.py:413-524)
