@@ -118,9 +118,11 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1
   return c;
 }
 
-// Top 24 bits of a Philox word as a float32 uniform in [0, 1) (exact).
-__device__ __forceinline__ float u24(uint32_t x) {
-  return __uint2float_rn(x >> 8) * 0x1.0p-24f;
+// Top 24 bits of a Philox word: the uniform u = (x >> 8) * 2^-24 in [0, 1),
+// kept scaled by 2^24 (an exact integer-valued float).  The LogSR decision
+// u < p* is evaluated as U < p* * 2^24; scaling by a power of two is exact.
+__device__ __forceinline__ float u24_scaled(uint32_t x) {
+  return __uint2float_rn(x >> 8);
 }
 
 // ---------------------------------------------------------------------------
@@ -156,13 +158,8 @@ __device__ void make_grid(double S_m, double S_v, double eps, LumaGrid* g) {
 // evaluates; each torch op of the reference is one correctly rounded fp32 op.
 // ---------------------------------------------------------------------------
 
-// torch.clamp_min / clamp keep NaN (ATen clamp kernels return NaN inputs).
-__device__ __forceinline__ float clamp_min_keepnan(float x, float lo) {
-  return isnan(x) ? x : fmaxf(x, lo);
-}
-__device__ __forceinline__ float clamp_keepnan(float x, float lo, float hi) {
-  return isnan(x) ? x : fminf(fmaxf(x, lo), hi);
-}
+// Clamps below keep NaN inputs as ATen's clamp kernels do (a NaN operand
+// fails every comparison and passes through the select unchanged).
 
 struct Consts {
   // step row
@@ -173,9 +170,10 @@ struct Consts {
   float n_sm32, n_dm, n_inv_dm, n_inv_zm, n_wmin, n_inv_wmin, n_dw, n_inv_dw, n_inv_zw;
   int n_dw_pos;
   int init;
-  // LogSR decision margins: kDecisionMargin where the series is valid,
-  // 2 (always take the exact path) where delta is too large for it
-  float margin_m, margin_w;
+  // LogSR decision on uniforms scaled by 2^24: inv_z * 2^24, and margins
+  // kDecisionMargin * 2^24 where the series is valid, 2^25 (always the exact
+  // path) where delta is too large for it
+  float inv_zm24, inv_zw24, margin_m, margin_w;
   // pass-1 approximate decode
   float o_dw_log2e;
   float tau_v;  // kBoundEps * eps^2
@@ -196,7 +194,8 @@ __device__ __forceinline__ float decode_m_lut(int q, const float* lut) {
 // v = (1.0 / w - eps).clamp_min(0).square()    functional.py:270
 __device__ __forceinline__ float decode_v(uint32_t qu, float wmin, float dw, float eps32) {
   const float w = __fmul_rn(wmin, expf(__fmul_rn((float)qu, dw)));
-  const float t = clamp_min_keepnan(__fsub_rn(__frcp_rn(w), eps32), 0.0f);
+  float t = __fsub_rn(__frcp_rn(w), eps32);
+  t = t < 0.0f ? 0.0f : t;  // clamp_min(0), NaN kept
   return __fmul_rn(t, t);
 }
 
@@ -235,42 +234,54 @@ __device__ __forceinline__ float adamw(const Consts& c, float p, float mn, float
 // exact expression.
 constexpr float kSeriesMaxDelta = 0.011f;
 constexpr float kDecisionMargin = 0x1.0p-19f;
+constexpr float kUScale = 0x1.0p24f;
 
-__device__ __forceinline__ float decision_margin(float delta) {
-  return delta <= kSeriesMaxDelta ? kDecisionMargin : 2.0f;
+// Margin on the 2^24-scaled scale.
+__host__ __device__ __forceinline__ float decision_margin(float delta) {
+  return delta <= kSeriesMaxDelta ? kDecisionMargin * kUScale : 2.0f * kUScale;
 }
 
-__device__ __forceinline__ bool logsr_up(float fr, float delta, float inv_z, float u, float margin) {
+// U = u * 2^24; inv_z24 = inv_z * 2^24; margin24 from decision_margin().
+// The series value and U are below 2^24, so the subtraction adds at most
+// 0.5 to the 5 (= 3e-7 * 2^24) series error bound, against a margin of 32.
+__device__ __forceinline__ bool logsr_up(float fr, float delta, float inv_z, float inv_z24,
+                                         float U, float margin24) {
   const float x = __fmul_rn(fr, delta);
   const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
-  const float diff = __fsub_rn(u, __fmul_rn(e, inv_z));
-  if (fabsf(diff) > margin) return diff < 0.0f;
-  return u < __fmul_rn(expm1f(x), inv_z);
+  const float diff = __fsub_rn(U, __fmul_rn(e, inv_z24));
+  if (fabsf(diff) > margin24) return diff < 0.0f;
+  return U < __fmul_rn(__fmul_rn(expm1f(x), inv_z), kUScale);
 }
 
 // _quantize_momentum (functional.py:133-150) with _log_sr (functional.py:38-67).
-__device__ __forceinline__ int quant_m(const Consts& c, float mn, float u) {
-  const float mc = clamp_keepnan(mn, -c.n_sm32, c.n_sm32);
-  const float y = __fmul_rn(log1pf(fabsf(mc)), c.n_inv_dm);
+// |m.clamp(-S_m, S_m)| = min(|m|, S_m) (NaN kept); y >= 0 because log1pf of a
+// non-negative value is non-negative, so of clamp(0, K_M) only the upper bound
+// can bite; sign(m_clip) * q is applied to the integer (for m = 0, q = 0).
+__device__ __forceinline__ int quant_m(const Consts& c, float mn, float U) {
+  const float a = fabsf(mn);
+  const float ac = a > c.n_sm32 ? c.n_sm32 : a;
+  const float y = __fmul_rn(log1pf(ac), c.n_inv_dm);
   const float fy = floorf(y);
   const float fr = __fsub_rn(y, fy);
-  float r = __fadd_rn(fy, logsr_up(fr, c.n_dm, c.n_inv_zm, u, c.margin_m) ? 1.0f : 0.0f);
-  r = clamp_keepnan(r, 0.0f, (float)LUMA_K_M);
-  const float sg = (mc > 0.0f) ? 1.0f : ((mc < 0.0f) ? -1.0f : 0.0f);
-  return (int)__fmul_rn(sg, r);
+  float r = __fadd_rn(fy, logsr_up(fr, c.n_dm, c.n_inv_zm, c.inv_zm24, U, c.margin_m) ? 1.0f : 0.0f);
+  r = r > (float)LUMA_K_M ? (float)LUMA_K_M : r;
+  const int ri = (int)r;
+  return mn < 0.0f ? -ri : ri;
 }
 
-// _quantize_preconditioner (functional.py:153-176) with _log_sr.
-__device__ __forceinline__ uint32_t quant_w(const Consts& c, float vn, float u) {
+// _quantize_preconditioner (functional.py:153-176) with _log_sr.  v' >= 0 (or
+// NaN), so v'.clamp_min(0) is the identity.
+__device__ __forceinline__ uint32_t quant_w(const Consts& c, float vn, float U) {
   // delta_w == 0 (_log_sr returns 0): inv_dw = 0 makes y = 0, frac = 0 and
   // p* = 0, so the expression below yields 0 without a branch.
-  const float den = __fadd_rn(__fsqrt_rn(clamp_min_keepnan(vn, 0.0f)), c.eps32);
-  const float w = clamp_keepnan(__frcp_rn(den), c.n_wmin, c.w_max);
+  const float den = __fadd_rn(__fsqrt_rn(vn), c.eps32);
+  float w = __frcp_rn(den);
+  w = w < c.n_wmin ? c.n_wmin : (w > c.w_max ? c.w_max : w);  // clamp, NaN kept
   const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
   const float fy = floorf(y);
   const float fr = __fsub_rn(y, fy);
-  float r = __fadd_rn(fy, logsr_up(fr, c.n_dw, c.n_inv_zw, u, c.margin_w) ? 1.0f : 0.0f);
-  r = clamp_keepnan(r, 0.0f, (float)LUMA_K_W);
+  float r = __fadd_rn(fy, logsr_up(fr, c.n_dw, c.n_inv_zw, c.inv_zw24, U, c.margin_w) ? 1.0f : 0.0f);
+  r = r < 0.0f ? 0.0f : (r > (float)LUMA_K_W ? (float)LUMA_K_W : r);  // clamp(0, K_W), NaN kept
   return (uint32_t)(int)r;  // .to(int32) then two's-complement wrap to int16
 }
 
@@ -758,10 +769,11 @@ __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Const
     if (injected) {
       load2<LUMA_F32>(d.u_m, e, both, vec, um0, um1);
       load2<LUMA_F32>(d.u_w, e, both, vec, uw0, uw1);
+      um0 *= kUScale; um1 *= kUScale; uw0 *= kUScale; uw1 *= kUScale;  // exact
     } else {
       const uint64_t ctr = ctr0 + (uint64_t)P;
       const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
-      um0 = u24(r.x); uw0 = u24(r.y); um1 = u24(r.z); uw1 = u24(r.w);
+      um0 = u24_scaled(r.x); uw0 = u24_scaled(r.y); um1 = u24_scaled(r.z); uw1 = u24_scaled(r.w);
     }
     pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
     pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
@@ -825,6 +837,8 @@ __device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Cons
     c.n_inv_dw = s.enc.inv_dw; c.n_inv_zw = s.enc.inv_zw; c.n_dw_pos = s.enc.dw_pos;
     c.margin_m = decision_margin(c.n_dm);
     c.margin_w = decision_margin(c.n_dw);
+    c.inv_zm24 = c.n_inv_zm * kUScale;
+    c.inv_zw24 = c.n_inv_zw * kUScale;
   } else {
     c.o_dw_log2e = c.o_dw * 1.44269504f;
     c.tau_v = kBoundEps * c.eps32 * c.eps32 + kTinyAbs;
@@ -969,13 +983,13 @@ __global__ void __launch_bounds__(kThreads) luma_quantize_kernel(
        P += (int64_t)gridDim.x * kThreads) {
     float um[2], uw[2];
     if (u_m != nullptr) {
-      um[0] = u_m[2 * P]; uw[0] = u_w[2 * P];
-      um[1] = (2 * P + 1 < n) ? u_m[2 * P + 1] : 0.0f;
-      uw[1] = (2 * P + 1 < n) ? u_w[2 * P + 1] : 0.0f;
+      um[0] = u_m[2 * P] * kUScale; uw[0] = u_w[2 * P] * kUScale;  // exact scaling
+      um[1] = (2 * P + 1 < n) ? u_m[2 * P + 1] * kUScale : 0.0f;
+      uw[1] = (2 * P + 1 < n) ? u_w[2 * P + 1] * kUScale : 0.0f;
     } else {
       const uint64_t ctr = ctr0 + (uint64_t)P;
       const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
-      um[0] = u24(r.x); uw[0] = u24(r.y); um[1] = u24(r.z); uw[1] = u24(r.w);
+      um[0] = u24_scaled(r.x); uw[0] = u24_scaled(r.y); um[1] = u24_scaled(r.z); uw[1] = u24_scaled(r.w);
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -1166,8 +1180,10 @@ int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid*
   c.n_sm32 = gr.s_m32; c.n_dm = gr.dm; c.n_inv_dm = gr.inv_dm; c.n_inv_zm = gr.inv_zm;
   c.n_wmin = gr.w_min; c.n_inv_wmin = gr.inv_wmin; c.n_dw = gr.dw; c.n_inv_dw = gr.inv_dw;
   c.n_inv_zw = gr.inv_zw; c.n_dw_pos = gr.dw_pos;
-  c.margin_m = gr.dm <= kSeriesMaxDelta ? kDecisionMargin : 2.0f;
-  c.margin_w = gr.dw <= kSeriesMaxDelta ? kDecisionMargin : 2.0f;
+  c.margin_m = decision_margin(gr.dm);
+  c.margin_w = decision_margin(gr.dw);
+  c.inv_zm24 = gr.inv_zm * kUScale;
+  c.inv_zw24 = gr.inv_zw * kUScale;
   const uint64_t sd = (uint64_t)seed;
   const int64_t n_pairs = (numel + 1) / 2;
   const int64_t want = (n_pairs + kThreads - 1) / kThreads;
