@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LUMA_ABI_VERSION 1
+#define LUMA_ABI_VERSION 2
 
 /* Quantization grid constants (reference config.py:23-25). */
 #define LUMA_K_M 32767        /* signed int16 magnitude of Q_m        */
@@ -163,6 +163,11 @@ typedef struct LumaStepArgs {
   void*                 events[3];    /* optional cudaEvent_t recorded before
                                          pass 1, between the passes and after
                                          pass 2 (timing); NULL to skip      */
+  int32_t               max_ctas;     /* 0: one CTA per SM; otherwise at most
+                                         this many CTAs, leaving SMs free for
+                                         work on other streams (e.g. an NCCL
+                                         all-gather of a previous bucket)   */
+  int32_t               reserved;
 } LumaStepArgs;
 
 /*

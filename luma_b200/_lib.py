@@ -16,7 +16,7 @@ import numpy as np
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libluma_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 LUMA_OK = 0
 LUMA_ERR_INVALID = 1
@@ -71,6 +71,8 @@ class LumaStepArgs(ctypes.Structure):
         ("total_octets", ctypes.c_int64),
         ("base_seed", ctypes.c_int64),
         ("events", ctypes.c_void_p * 3),
+        ("max_ctas", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 

@@ -38,6 +38,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 static_assert(sizeof(LumaTensorDesc) == 96, "LumaTensorDesc layout");
 static_assert(sizeof(LumaStepRow) == 56, "LumaStepRow layout");
@@ -741,11 +742,52 @@ __device__ __forceinline__ void load_raw_pair(const LumaTensorDesc& d, bool init
   }
 }
 
-// Pass 2 over pairs [p_lo, p_hi) of a tensor: pair P holds elements 2P, 2P+1
-// and draws Philox block (rng_offset / 2 + P).  The next pair's loads are
-// issued before the current pair is computed.
+// Pass 2 over pairs [p_lo, p_hi) of a tensor, any alignment, injected or
+// Philox uniforms, partial last pair: pair P holds elements 2P, 2P+1 and
+// draws Philox block (rng_offset / 2 + P).  The steady state of aligned
+// tensors runs in pass2_fast below.
 template <int PD, int GD>
 __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Consts& c,
+                                            const float* lut, uint32_t k0, uint32_t k1, bool vec2,
+                                            int64_t p_lo, int64_t p_hi) {
+  constexpr int kThreads = kThreadsPass2;
+  const bool injected = d.u_m != nullptr;
+  const uint64_t ctr0 = (uint64_t)d.rng_offset >> 1;
+  for (int64_t P = p_lo + threadIdx.x; P < p_hi; P += kThreads) {
+    RawPair cur;
+    load_raw_pair<PD, GD>(d, c.init, vec2, P, cur);
+    const int64_t e = 2 * P;
+    const bool both = e + 1 < d.numel;
+    const bool vec = vec2 && both;
+    float p0, p1, g0, g1;
+    unpack2<PD>(cur.p, p0, p1);
+    unpack2<GD>(cur.g, g0, g1);
+    uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
+    uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
+    float um0, um1, uw0, uw1;
+    if (injected) {
+      load2<LUMA_F32>(d.u_m, e, both, vec, um0, um1);
+      load2<LUMA_F32>(d.u_w, e, both, vec, uw0, uw1);
+      um0 *= kUScale; um1 *= kUScale; uw0 *= kUScale; uw1 *= kUScale;  // exact
+    } else {
+      const uint64_t ctr = ctr0 + (uint64_t)P;
+      const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+      um0 = u24_scaled(r.x); uw0 = u24_scaled(r.y); um1 = u24_scaled(r.z); uw1 = u24_scaled(r.w);
+    }
+    pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
+    pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
+    store2<PD>(d.param, e, both, vec, p0, p1);
+    store2_codes(d.q_m, e, both, vec, qm0, qm1);
+    store2_codes(d.q_w, e, both, vec, qw0, qw1);
+  }
+}
+
+// Pass 2 over pairs [p_lo, p_hi) of a tensor, prefetching: pair P holds
+// elements 2P, 2P+1 and draws Philox block (rng_offset / 2 + P); the next
+// pair's loads are issued before the current pair is computed.  Used for bf16
+// params, where it measured faster than pass2_fast.
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_prefetch(const LumaTensorDesc& d, const Consts& c,
                                             const float* lut, uint32_t k0, uint32_t k1, bool vec2,
                                             int64_t p_lo, int64_t p_hi) {
   constexpr int kThreads = kThreadsPass2;
@@ -784,6 +826,87 @@ __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Const
   }
 }
 
+// Steady-state pass 2 over n complete, 16-byte-aligned pairs with Philox
+// uniforms: pair-typed pointers to the first pair, 32-bit indices, no
+// per-pair tail or alignment tests.  Same arithmetic as pass2_pairs.
+template <int DT>
+struct PairWord {  // one pair of a stream as a single load/store unit
+  using T = typename std::conditional<DT == LUMA_F32, uint2, uint32_t>::type;
+};
+
+template <int DT>
+__device__ __forceinline__ void to_words(const typename PairWord<DT>::T& v, uint32_t (&w)[2]) {
+  if constexpr (DT == LUMA_F32) { w[0] = v.x; w[1] = v.y; } else { w[0] = v; w[1] = 0u; }
+}
+
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_fast(const Consts& c, const float* lut, uint32_t k0,
+                                           uint32_t k1, typename PairWord<PD>::T* pp,
+                                           const typename PairWord<GD>::T* gp, uint32_t* qmp,
+                                           uint32_t* qwp, uint64_t ctr_base, int n) {
+  constexpr int kThreads = kThreadsPass2;
+  int i = threadIdx.x;
+  RawPair cur;
+  auto load = [&](int j, RawPair& r) {
+    to_words<PD>(__ldcs(pp + j), r.p);
+    to_words<GD>(__ldcs(gp + j), r.g);
+    r.qm = c.init ? 0u : __ldcs(qmp + j);
+    r.qw = c.init ? 0u : __ldcs(qwp + j);
+  };
+  if (i < n) load(i, cur);
+  for (; i < n; i += kThreads) {
+    RawPair nxt;
+    if (i + kThreads < n) load(i + kThreads, nxt);
+    float p0, p1, g0, g1;
+    unpack2<PD>(cur.p, p0, p1);
+    unpack2<GD>(cur.g, g0, g1);
+    uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
+    uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
+    const uint64_t ctr = ctr_base + (uint32_t)i;
+    const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+    const float um0 = u24_scaled(r.x), uw0 = u24_scaled(r.y);
+    const float um1 = u24_scaled(r.z), uw1 = u24_scaled(r.w);
+    pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
+    pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
+    if constexpr (PD == LUMA_F32) {
+      __stcs(pp + i, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
+    } else {
+      __stcs(pp + i, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
+                         ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p1)) << 16));
+    }
+    __stcs(qmp + i, (qm0 & 0xFFFFu) | (qm1 << 16));
+    __stcs(qwp + i, (qw0 & 0xFFFFu) | (qw1 << 16));
+    cur = nxt;
+  }
+}
+
+// Pass 2 for one tensor segment.  bf16 params: the prefetching pair loop.
+// fp32 params: the steady-state loop where it applies, the general loop
+// otherwise (unaligned views, injected uniforms, the odd tail).  The choice
+// per param dtype is measured (one Llama-3-8B layer and GPT-2 small).
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_segment(const LumaTensorDesc& d, const Consts& c,
+                                              const float* lut, uint32_t k0, uint32_t k1,
+                                              bool vec2, int64_t p_lo, int64_t p_hi) {
+  if constexpr (PD == LUMA_BF16) {
+    pass2_prefetch<PD, GD>(d, c, lut, k0, k1, vec2, p_lo, p_hi);
+    return;
+  }
+  const int64_t p_full = min(p_hi, d.numel / 2);  // pairs with both elements
+  if (vec2 && d.u_m == nullptr && p_full > p_lo && p_full - p_lo <= 0x7FFFFFFF) {
+    using PW = typename PairWord<PD>::T;
+    using GW = typename PairWord<GD>::T;
+    pass2_fast<PD, GD>(c, lut, k0, k1, static_cast<PW*>(d.param) + p_lo,
+                       static_cast<const GW*>(d.grad) + p_lo,
+                       reinterpret_cast<uint32_t*>(d.q_m) + p_lo,
+                       reinterpret_cast<uint32_t*>(d.q_w) + p_lo,
+                       ((uint64_t)d.rng_offset >> 1) + (uint64_t)p_lo, (int)(p_full - p_lo));
+    if (p_full < p_hi) pass2_pairs<PD, GD>(d, c, lut, k0, k1, vec2, p_full, p_hi);
+  } else {
+    pass2_pairs<PD, GD>(d, c, lut, k0, k1, vec2, p_lo, p_hi);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Kernels
 // ---------------------------------------------------------------------------
@@ -794,15 +917,15 @@ __device__ __forceinline__ void dispatch_pass2(const LumaTensorDesc& d, const Co
                                                bool vec2, int64_t p_lo, int64_t p_hi) {
   if (d.param_dtype == LUMA_F32) {
     switch (d.grad_dtype) {
-      case LUMA_F32: pass2_pairs<LUMA_F32, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      case LUMA_BF16: pass2_pairs<LUMA_F32, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      default: pass2_pairs<LUMA_F32, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_F32: pass2_segment<LUMA_F32, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_segment<LUMA_F32, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_segment<LUMA_F32, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
     }
   } else {
     switch (d.grad_dtype) {
-      case LUMA_F32: pass2_pairs<LUMA_BF16, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      case LUMA_BF16: pass2_pairs<LUMA_BF16, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      default: pass2_pairs<LUMA_BF16, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_F32: pass2_segment<LUMA_BF16, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_segment<LUMA_BF16, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_segment<LUMA_BF16, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
     }
   }
 }
@@ -1062,6 +1185,11 @@ int device_info(DeviceInfo** out) {
   return LUMA_OK;
 }
 
+// max_ctas from LumaStepArgs: 0 = the device default
+int cap(int device_ctas, int32_t max_ctas) {
+  return (max_ctas > 0 && max_ctas < device_ctas) ? max_ctas : device_ctas;
+}
+
 int grid_for(int64_t total_octets, int threads, int max_ctas) {
   // at least one full tile (one octet per thread) per CTA
   const int64_t want = (total_octets + threads - 1) / threads;
@@ -1104,9 +1232,10 @@ int luma_step(const LumaStepArgs* args, void* stream) {
   g_err[0] = '\0';
   if (args == nullptr) return fail(LUMA_ERR_INVALID, "luma_step: args is NULL");
   const LumaStepArgs a = *args;
-  if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0)
-    return fail(LUMA_ERR_INVALID, "luma_step: negative size (n_desc=%d n_rows=%d total_octets=%lld)",
-                a.n_desc, a.n_rows, (long long)a.total_octets);
+  if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0 || a.max_ctas < 0)
+    return fail(LUMA_ERR_INVALID,
+                "luma_step: negative size (n_desc=%d n_rows=%d total_octets=%lld max_ctas=%d)",
+                a.n_desc, a.n_rows, (long long)a.total_octets, a.max_ctas);
   if (a.n_desc == 0 || a.total_octets == 0) return LUMA_OK;
   if (a.descs == nullptr || a.slots == nullptr || a.rows == nullptr || a.n_rows == 0)
     return fail(LUMA_ERR_INVALID, "luma_step: descs/slots/rows must be non-NULL and n_rows > 0");
@@ -1119,7 +1248,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[0]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  luma_pass_kernel<false><<<grid_for(a.total_octets, kThreadsPass1, di->ctas_pass1), kThreadsPass1,
+  luma_pass_kernel<false><<<grid_for(a.total_octets, kThreadsPass1, cap(di->ctas_pass1, a.max_ctas)), kThreadsPass1,
                             kLutBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 1");
@@ -1127,7 +1256,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[1]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  luma_pass_kernel<true><<<grid_for(a.total_octets, kThreadsPass2, di->ctas_pass2), kThreadsPass2,
+  luma_pass_kernel<true><<<grid_for(a.total_octets, kThreadsPass2, cap(di->ctas_pass2, a.max_ctas)), kThreadsPass2,
                            kLutBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
@@ -1200,10 +1329,11 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
   g_err[0] = '\0';
   if (args == nullptr) return fail(LUMA_ERR_INVALID, "luma_step_noalloc: args is NULL");
   const LumaStepArgs a = *args;
-  if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0)
+  if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0 || a.max_ctas < 0)
     return fail(LUMA_ERR_INVALID,
-                "luma_step_noalloc: negative size (n_desc=%d n_rows=%d total_octets=%lld)",
-                a.n_desc, a.n_rows, (long long)a.total_octets);
+                "luma_step_noalloc: negative size (n_desc=%d n_rows=%d total_octets=%lld "
+                "max_ctas=%d)",
+                a.n_desc, a.n_rows, (long long)a.total_octets, a.max_ctas);
   if (a.n_desc > LUMA_NOALLOC_MAX_DESCS)
     return fail(LUMA_ERR_INVALID,
                 "luma_step_noalloc: %d tensors exceed the built-in scratch of %d; use luma_step "
@@ -1228,7 +1358,7 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[0]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  luma_pass_kernel<false, true><<<grid_for(a.total_octets, kThreadsPass1, di->ctas_pass1),
+  luma_pass_kernel<false, true><<<grid_for(a.total_octets, kThreadsPass1, cap(di->ctas_pass1, a.max_ctas)),
                                   kThreadsPass1, kLutBytes, s>>>(a, 1, acc);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 1 (noalloc)");
@@ -1236,7 +1366,7 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[1]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
-  luma_pass_kernel<true, true><<<grid_for(a.total_octets, kThreadsPass2, di->ctas_pass2),
+  luma_pass_kernel<true, true><<<grid_for(a.total_octets, kThreadsPass2, cap(di->ctas_pass2, a.max_ctas)),
                                  kThreadsPass2, kLutBytes, s>>>(a, 1, acc);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2 (noalloc)");

@@ -144,7 +144,7 @@ class DeviceEngine:
             ev.record(stream)
 
     def step(self, segs: list[Segment], rows: np.ndarray, base_seed: int,
-             stream: torch.cuda.Stream | None = None, events=None) -> None:
+             stream: torch.cuda.Stream | None = None, events=None, max_ctas: int = 0) -> None:
         if not segs:
             return
         if stream is None:
@@ -167,5 +167,6 @@ class DeviceEngine:
         a.base_seed = ctypes.c_int64(int(base_seed)).value
         for i in range(3):
             a.events[i] = None if events is None else events[i]
+        a.max_ctas = max_ctas
         _lib.check(_lib.lib().luma_step(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)),
                    "luma_step")

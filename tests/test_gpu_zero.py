@@ -28,7 +28,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, pdt_name, out_q):
+def _worker(rank, world, port, pdt_name, buckets, out_q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "tests")]
@@ -45,13 +45,13 @@ def _worker(rank, world, port, pdt_name, out_q):
     try:
         pdt = getattr(torch, pdt_name)
         numels = [int(torch.tensor(s).prod()) if s else 1 for s in SHAPES]
-        lay = plan_layout(numels, world)
+        lay = plan_layout(numels, world, buckets)
         gen = torch.Generator().manual_seed(5)
         flat = torch.zeros(lay.total, dtype=pdt, device=dev)
         for v, s in zip(flat_views(flat, lay, SHAPES), SHAPES):
             v.copy_((torch.randn(s, generator=gen) * 0.02).to(pdt))
         segs = shard_segments(lay, rank)
-        opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123)
+        opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, max_ctas=100)
         # oracle: every local segment as its own tensor
         oparams = [flat[sg.flat:sg.flat + sg.length].clone() for sg in segs]
         for p in oparams:
@@ -66,15 +66,14 @@ def _worker(rank, world, port, pdt_name, out_q):
         orc = OracleLUMA(oparams, lr=1e-3, draws=draws)
         for t in range(1, 4):
             gfull = (torch.randn(lay.total, generator=gen) * 1e-3).to(torch.bfloat16).to(dev)
-            gshard = gfull[rank * lay.shard:(rank + 1) * lay.shard].contiguous()
+            gshard = torch.cat([gfull[slice(*lay.owned(rank, b))] for b in range(lay.buckets)])
             for k, sg in enumerate(segs):
                 oparams[k].grad = gfull[sg.flat:sg.flat + sg.length].clone()
             opt.step(gshard)
             orc.step()
             torch.cuda.synchronize()
-            base = rank * lay.shard
             for k, sg in enumerate(segs):
-                lo = sg.flat - base
+                lo = sg.local
                 if not torch.equal(flat[sg.flat:sg.flat + sg.length], oparams[k]):
                     msgs.append(f"t={t} seg {k}: params differ")
                 ost = orc.state[id(oparams[k])]
@@ -98,13 +97,14 @@ def _worker(rank, world, port, pdt_name, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("pdt_name", ["bfloat16", "float32"])
-def test_zero_sharded_step_two_gpus(pdt_name):
+@pytest.mark.parametrize("pdt_name,buckets", [("bfloat16", 1), ("float32", 1), ("bfloat16", 3)])
+def test_zero_sharded_step_two_gpus(pdt_name, buckets):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, pdt_name, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, pdt_name, buckets, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=600) for _ in range(world))

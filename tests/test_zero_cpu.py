@@ -27,19 +27,26 @@ def llama_like_numels():
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("buckets", [1, 3, 8])
 @pytest.mark.parametrize("numels", [llama_like_numels(), [1, 7, 8, 9, 1025, 3, 0, 17],
                                     list(np.random.default_rng(0).integers(1, 5000, 300))])
-def test_segments_partition_every_tensor(world, numels):
-    lay = plan_layout(numels, world)
-    assert lay.shard % ALIGN == 0 and lay.total >= sum(-(-n // ALIGN) * ALIGN for n in numels)
+def test_segments_partition_every_tensor(world, buckets, numels):
+    lay = plan_layout(numels, world, buckets)
+    assert lay.piece % ALIGN == 0 and lay.total >= sum(-(-n // ALIGN) * ALIGN for n in numels)
+    assert lay.shard == buckets * lay.piece and lay.total == world * lay.shard
     assert all(s % ALIGN == 0 for s in lay.starts)
     covered = [np.zeros(n, dtype=np.int32) for n in numels]
     for r in range(world):
+        local = np.zeros(lay.shard, dtype=np.int32)
         for sg in shard_segments(lay, r):
-            assert r * lay.shard <= sg.flat and sg.flat + sg.length <= (r + 1) * lay.shard
-            assert sg.offset % ALIGN == 0 and sg.flat % ALIGN == 0
+            lo, hi = lay.owned(r, sg.bucket)
+            assert lo <= sg.flat and sg.flat + sg.length <= hi
+            assert sg.local == sg.bucket * lay.piece + (sg.flat - lo)
+            assert sg.offset % ALIGN == 0 and sg.flat % ALIGN == 0 and sg.local % ALIGN == 0
             assert sg.flat == lay.starts[sg.tensor] + sg.offset
             covered[sg.tensor][sg.offset:sg.offset + sg.length] += 1
+            local[sg.local:sg.local + sg.length] += 1
+        assert local.max() <= 1
     for c in covered:
         assert np.all(c == 1)
 
@@ -62,20 +69,21 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _gather_worker(rank, world, port, numels, out_q):
+def _gather_worker(rank, world, port, numels, buckets, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        lay = plan_layout(numels, world)
+        lay = plan_layout(numels, world, buckets)
         flat = torch.full((lay.total,), -1.0)
         # "step": this rank writes a known value into every element it owns
         for sg in shard_segments(lay, rank):
             flat[sg.flat:sg.flat + sg.length] = torch.arange(sg.length, dtype=torch.float32) + \
                 1000.0 * sg.tensor + sg.offset
-        shard = flat[rank * lay.shard:(rank + 1) * lay.shard].clone()
-        out = torch.empty_like(flat)
-        dist.all_gather_into_tensor(out, shard)
+        out = flat.clone()
+        for b in range(buckets):  # per-bucket in-place gather, as ZeroLUMA.gather does
+            lo, hi = lay.owned(rank, b)
+            dist.all_gather_into_tensor(out[b * lay.span:(b + 1) * lay.span], out[lo:hi].clone())
         ok = True
         for t, (n, s) in enumerate(zip(lay.numels, lay.starts)):
             want = torch.arange(n, dtype=torch.float32) + 1000.0 * t
@@ -85,13 +93,14 @@ def _gather_worker(rank, world, port, numels, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_gather_rebuilds_params_gloo(world):
+@pytest.mark.parametrize("world,buckets", [(2, 1), (2, 3)])
+def test_gather_rebuilds_params_gloo(world, buckets):
     numels = [37, 1024, 5, 999, 64]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, numels, q)) for r in range(world)]
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, numels, buckets, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
