@@ -435,73 +435,73 @@ __device__ __forceinline__ void store8_codes(int16_t* base, int64_t e0, int n, b
 // Per-tensor segment bodies
 // ---------------------------------------------------------------------------
 
-// Raw words of one octet of grad and codes (grad: 8 words for fp32, 4 for
-// 16-bit types; codes: 4 words each), kept packed for prefetching.
-struct RawOctet {
-  uint32_t g[8], qm[4], qw[4];
+// Running state of the pass-1 maximum search of one tensor segment.
+//   am/av: this thread's exact max |m'| / max v' (float bit patterns);
+//   Tm/Tv: warp-wide lower bounds of the maxima from earlier iterations;
+//   lm/lv: this thread's running lower bounds (they include the element under
+//          test, whose own bound never excludes it).
+struct MaxSearch {
+  uint32_t am = 0u, av = 0u;
+  float Tm = 0.0f, Tv = 0.0f, lm = 0.0f, lv = 0.0f;
+
+  // Fold the thread bounds into the warp-wide ones (all 32 lanes call this).
+  __device__ __forceinline__ void warp_sync_bounds() {
+    Tm = fmaxf(Tm, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lm))));
+    Tv = fmaxf(Tv, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lv))));
+  }
 };
 
-// Loads octet o (if o < o_hi) and returns its element count (0 if none).
-template <int GD>
-__device__ __forceinline__ int load_raw_octet(const LumaTensorDesc& d, int64_t o, int64_t o_hi,
-                                              RawOctet& r) {
-  if (o >= o_hi) return 0;
-  const int64_t e0 = o * 8;
-  const int64_t rem = d.numel - e0;
-  const int n = rem < 8 ? (int)rem : 8;
-  if (d.vec_ok != 0 && n == 8) {
-    if (GD == LUMA_F32) {
-      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(d.grad) + e0);
-      const uint4 a = __ldcs(p), b = __ldcs(p + 1);
-      r.g[0] = a.x; r.g[1] = a.y; r.g[2] = a.z; r.g[3] = a.w;
-      r.g[4] = b.x; r.g[5] = b.y; r.g[6] = b.z; r.g[7] = b.w;
-    } else {
-      const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(d.grad) + e0));
-      r.g[0] = a.x; r.g[1] = a.y; r.g[2] = a.z; r.g[3] = a.w;
-    }
-    const uint4 m = __ldcs(reinterpret_cast<const uint4*>(d.q_m + e0));
-    const uint4 w = __ldcs(reinterpret_cast<const uint4*>(d.q_w + e0));
-    r.qm[0] = m.x; r.qm[1] = m.y; r.qm[2] = m.z; r.qm[3] = m.w;
-    r.qw[0] = w.x; r.qw[1] = w.y; r.qw[2] = w.z; r.qw[3] = w.w;
+// One element of pass 1 (step >= 2): exact |m'| from the decode table when
+// there is one, certified-bound candidates otherwise; v' by certified bounds.
+__device__ __forceinline__ void pass1_elem(const Consts& c, const float* lut, float g, int q,
+                                           uint32_t qw, MaxSearch& ms) {
+  if (lut != nullptr) {
+    // exact |m'| from the decode table (functional.py:274, 282)
+    const float mne = __fadd_rn(__fmul_rn(c.beta1, decode_m_lut(q, lut)), __fmul_rn(c.omb1, g));
+    ms.am = max(ms.am, __float_as_uint(fabsf(mne)));
+  } else if (q == 0 || c.beta1 == 0.0f) {
+    // fl(beta1 * 0) = 0, so m' = fl(c1 g) exactly
+    const float mne = fabsf(__fmul_rn(c.omb1, g));
+    ms.am = max(ms.am, __float_as_uint(mne));
+    ms.lm = fmaxf(ms.lm, mne);
   } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const bool in = j < n;
-      if (GD == LUMA_F32) {
-        r.g[j] = in ? static_cast<const uint32_t*>(d.grad)[e0 + j] : 0u;
-      } else {
-        const uint32_t h = in ? static_cast<const uint16_t*>(d.grad)[e0 + j] : 0u;
-        r.g[j >> 1] = (j & 1) ? (r.g[j >> 1] | (h << 16)) : h;
-      }
-      const uint32_t a = in ? (uint16_t)d.q_m[e0 + j] : 0u;
-      const uint32_t b = in ? (uint16_t)d.q_w[e0 + j] : 0u;
-      r.qm[j >> 1] = (j & 1) ? (r.qm[j >> 1] | (a << 16)) : a;
-      r.qw[j >> 1] = (j & 1) ? (r.qw[j >> 1] | (b << 16)) : b;
+    const float e = expm1_approx(__fmul_rn((float)abs(q), c.o_dm));
+    const float bm = c.beta1 * (q < 0 ? -e : e);
+    const float mn = fabsf(bm + c.omb1 * g);
+    const float bnd_m = kBoundEps * (fabsf(bm) + mn) + kTinyAbs;
+    const float um = mn + bnd_m;
+    ms.lm = fmaxf(ms.lm, mn - bnd_m);
+    if (!(um <= __uint_as_float(ms.am)) && !(um < fmaxf(ms.Tm, ms.lm))) {
+      // exact |m'| (functional.py:274, 282)
+      const float mx = decode_m(q, c.o_dm);
+      const float mne = __fadd_rn(__fmul_rn(c.beta1, mx), __fmul_rn(c.omb1, g));
+      ms.am = max(ms.am, __float_as_uint(fabsf(mne)));
     }
   }
-  return n;
-}
-
-template <int GD>
-__device__ __forceinline__ void unpack8(const uint32_t (&w)[8], float (&x)[8]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (GD == LUMA_F32) {
-      x[j] = __uint_as_float(w[j]);
-    } else {
-      const uint32_t h = (w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
-      x[j] = (GD == LUMA_BF16) ? __uint_as_float(h << 16)
-                               : __half2float(__ushort_as_half((unsigned short)h));
-    }
+  const float w = c.o_wmin * ex2_approx((float)qw * c.o_dw_log2e);
+  const float t = fmaxf(rcp_approx(w) - c.eps32, 0.0f);
+  const float vn = c.beta2 * (t * t) + c.omb2 * (g * g);
+  const float bnd_v = kBoundEps * vn + c.tau_v;
+  const float uv = vn + bnd_v;
+  ms.lv = fmaxf(ms.lv, vn - bnd_v);
+  if (!(uv <= __uint_as_float(ms.av)) && !(uv < fmaxf(ms.Tv, ms.lv))) {
+    // exact v' (functional.py:270, 275, 282)
+    const float v = decode_v(qw, c.o_wmin, c.o_dw, c.eps32);
+    const float vne = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, __fmul_rn(g, g)));
+    ms.av = max(ms.av, __float_as_uint(vne));
   }
 }
 
-// Pass 1 body: this thread's exact max |m'| and max v' bit patterns.  All
-// threads of the CTA run the same number of iterations (warp reductions).
+// Pass 1 over octets [o_lo, o_hi): one octet per thread per iteration, loaded
+// straight into registers (16-byte loads when aligned).  Staging tiles through
+// shared memory with bulk copies measured slower on B200 (the block barriers
+// per tile cost more than the latency they hide at 32 warps per SM), and so did
+// prefetching the next octet into registers (it spilled).  All threads run the
+// same number of iterations (warp reductions).
 template <int GD>
 __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Consts& c,
                                              const float* lut, int64_t o_lo, int64_t o_hi,
-                                             uint32_t& am, uint32_t& av) {
+                                             MaxSearch& ms) {
   constexpr int kThreads = kThreadsPass1;
   if (c.init) {  // first step: m' = (1-b1) g, v' = (1-b2) g^2, cheap and exact
     for (int64_t o = o_lo + threadIdx.x; o < o_hi; o += kThreads) {
@@ -515,75 +515,33 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
         if (j < n) {
           float mn, vn;
           ema(c, g[j], 0.0f, 0.0f, mn, vn);
-          am = max(am, __float_as_uint(fabsf(mn)));
-          av = max(av, __float_as_uint(vn));
+          ms.am = max(ms.am, __float_as_uint(fabsf(mn)));
+          ms.av = max(ms.av, __float_as_uint(vn));
         }
       }
     }
     return;
   }
-  // Tm/Tv: warp-wide lower bounds of the maxima from earlier iterations;
-  // lm/lv: this thread's running lower bounds (they include the element
-  // under test, whose own bound never excludes it).  The next octet's raw
-  // words are loaded before the current octet is evaluated.
-  float Tm = 0.0f, Tv = 0.0f, lm = 0.0f, lv = 0.0f;
-  RawOctet cur;
-  int n_cur = load_raw_octet<GD>(d, o_lo + threadIdx.x, o_hi, cur);
   for (int64_t ob = o_lo; ob < o_hi; ob += kThreads) {
-    RawOctet nxt;
-    const int n_nxt = load_raw_octet<GD>(d, ob + kThreads + threadIdx.x, o_hi, nxt);
-    const int n = n_cur;
-    if (n > 0) {
-      float g[8];
-      unpack8<GD>(cur.g, g);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j < n) {
-          const int q = (int)(int16_t)(uint16_t)(cur.qm[j >> 1] >> (16 * (j & 1)));
-          const uint32_t qwj = (cur.qw[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
-          if (lut != nullptr) {
-            // exact |m'| from the decode table (functional.py:274, 282)
-            const float mne = __fadd_rn(__fmul_rn(c.beta1, decode_m_lut(q, lut)),
-                                        __fmul_rn(c.omb1, g[j]));
-            am = max(am, __float_as_uint(fabsf(mne)));
-          } else if (q == 0 || c.beta1 == 0.0f) {
-            // fl(beta1 * 0) = 0, so m' = fl(c1 g) exactly
-            const float mne = fabsf(__fmul_rn(c.omb1, g[j]));
-            am = max(am, __float_as_uint(mne));
-            lm = fmaxf(lm, mne);
-          } else {
-            const float e = expm1_approx(__fmul_rn((float)abs(q), c.o_dm));
-            const float bm = c.beta1 * (q < 0 ? -e : e);
-            const float mn = fabsf(bm + c.omb1 * g[j]);
-            const float bnd_m = kBoundEps * (fabsf(bm) + mn) + kTinyAbs;
-            const float um = mn + bnd_m;
-            lm = fmaxf(lm, mn - bnd_m);
-            if (!(um <= __uint_as_float(am)) && !(um < fmaxf(Tm, lm))) {
-              // exact |m'| (functional.py:274, 282)
-              const float mx = decode_m(q, c.o_dm);
-              const float mne = __fadd_rn(__fmul_rn(c.beta1, mx), __fmul_rn(c.omb1, g[j]));
-              am = max(am, __float_as_uint(fabsf(mne)));
-            }
-          }
-          const float w = c.o_wmin * ex2_approx((float)qwj * c.o_dw_log2e);
-          const float t = fmaxf(rcp_approx(w) - c.eps32, 0.0f);
-          const float vn = c.beta2 * (t * t) + c.omb2 * (g[j] * g[j]);
-          const float bnd_v = kBoundEps * vn + c.tau_v;
-          const float uv = vn + bnd_v;
-          lv = fmaxf(lv, vn - bnd_v);
-          if (!(uv <= __uint_as_float(av)) && !(uv < fmaxf(Tv, lv))) {
-            // exact v' (functional.py:270, 275, 282)
-            const float v = decode_v(qwj, c.o_wmin, c.o_dw, c.eps32);
-            const float vne = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, __fmul_rn(g[j], g[j])));
-            av = max(av, __float_as_uint(vne));
-          }
-        }
-      }
+    const int64_t o = ob + threadIdx.x;
+    const int64_t e0 = o * 8;
+    int n = 0;
+    if (o < o_hi) {
+      const int64_t rem = d.numel - e0;
+      n = rem < 8 ? (int)rem : 8;
     }
-    Tm = fmaxf(Tm, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lm))));
-    Tv = fmaxf(Tv, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lv))));
-    cur = nxt;
-    n_cur = n_nxt;
+    if (n > 0) {
+      const bool vec = d.vec_ok != 0 && n == 8;
+      float g[8];
+      uint16_t qm[8], qw[8];
+      load8<GD>(d.grad, e0, n, vec, g);
+      load8_codes(d.q_m, e0, n, vec, qm);
+      load8_codes(d.q_w, e0, n, vec, qw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j < n) pass1_elem(c, lut, g[j], (int)(int16_t)qm[j], (uint32_t)qw[j], ms);
+    }
+    ms.warp_sync_bounds();
   }
 }
 
@@ -1023,12 +981,13 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
     }
 
     if (!PASS2) {
-      uint32_t am = 0u, av = 0u;
+      MaxSearch ms;
       switch (d.grad_dtype) {
-        case LUMA_F32: pass1_octets<LUMA_F32>(d, c, lut, o_lo, o_hi, am, av); break;
-        case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, lut, o_lo, o_hi, am, av); break;
-        default: pass1_octets<LUMA_F16>(d, c, lut, o_lo, o_hi, am, av); break;
+        case LUMA_F32: pass1_octets<LUMA_F32>(d, c, lut, o_lo, o_hi, ms); break;
+        case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, lut, o_lo, o_hi, ms); break;
+        default: pass1_octets<LUMA_F16>(d, c, lut, o_lo, o_hi, ms); break;
       }
+      uint32_t am = ms.am, av = ms.av;
       am = __reduce_max_sync(0xffffffffu, am);
       av = __reduce_max_sync(0xffffffffu, av);
       const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

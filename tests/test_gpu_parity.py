@@ -183,6 +183,13 @@ def test_large_tensor_across_many_ctas_bit_exact():
     _run_pair([(5_000_003,), (3,), (70_001,)], torch.bfloat16, [torch.bfloat16], steps=2, gscale=1e-3)
 
 
+def test_long_segments_table_and_bulk_tiles_bit_exact():
+    """Segments long enough for the decode table and the bulk-copied pass-1
+    tiles on every CTA, one tensor per grad dtype, ragged lengths."""
+    _run_pair([(12_000_011,), (11_999_993,), (12_000_000,)], torch.float32,
+              [torch.float32, torch.float16, torch.bfloat16], steps=3, gscale=1e-3)
+
+
 def test_export_decode_bit_exact():
     opt, pk = _run_pair([(3000,), (64, 64)], torch.float32, [torch.float32], steps=3)
     exp = opt.export_adamw_state()
