@@ -369,7 +369,7 @@ def run_zero(args, rank, world, local_rank):
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     max_ctas = max(1, sms - args.reserve_sms) if args.reserve_sms > 0 else 0
     opt = ZeroLUMA(flat, lay, rank, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
-                   base_seed=1234, max_ctas=max_ctas)
+                   base_seed=1234, max_ctas=max_ctas, gather=args.gather)
     for _ in range(max(args.warmup, 1)):
         opt.step(gshard)
     torch.cuda.synchronize()
@@ -419,6 +419,7 @@ def run_zero(args, rank, world, local_rank):
                "h2d_bytes_per_step": host.numel() * host.element_size(),
                "d2h_bytes_per_step": sum(e.slots.numel() for e in opt.engines), "steps": E}
 
+    opt.close()
     p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
     peak, peak_kind = measured_peak()
     # pass-2 share of the local step, from the single-GPU split (pass 2 ~ 83%):
@@ -432,6 +433,7 @@ def run_zero(args, rank, world, local_rank):
         "overlap_saving_ms": round(ms_local + ms_gather - ms_step, 3),
         "step_only_gparams": round(n_params / (ms_local * 1e-3) / 1e9, 3),
         "shard_params": lay.shard, "buckets": lay.buckets, "max_ctas": max_ctas,
+        "gather": args.gather,
         "bytes_per_param": p1b + p2b, "pass2_bytes_per_param": p2b,
         "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<false>+<true> (local step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -464,7 +466,7 @@ def result_line(args, res, world, scaling, dtype, config_out):
             "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
             "gpu_launches": res["gpu_launches"]}
     for key in ("local_step_ms", "allgather_ms", "allgather_gbs_per_rank", "overlap_saving_ms",
-                "step_only_gparams", "shard_params", "buckets", "max_ctas"):
+                "step_only_gparams", "shard_params", "buckets", "max_ctas", "gather"):
         if key in res:
             line[key] = res[key]
     return line
@@ -481,8 +483,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--buckets", type=int, default=8,
                     help="N>1: gather buckets (each bucket's gather overlaps the next's kernels)")
-    ap.add_argument("--reserve-sms", type=int, default=16,
-                    help="N>1: SMs left free for NCCL while a gather is in flight")
+    ap.add_argument("--reserve-sms", type=int, default=0,
+                    help="N>1, NCCL gather: SMs left free for NCCL while a gather is in flight")
+    ap.add_argument("--gather", default="copy", choices=["nccl", "copy"],
+                    help="N>1: post-step all-gather by NCCL or by copy-engine pushes over CUDA IPC")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -517,7 +521,9 @@ def main():
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
                                              timeout=datetime.timedelta(seconds=300))
         res = run_zero(args, rank, world, local_rank)
-        config_out["parallelism"] = f"zero1-dp{world} (flat shards, per-shard scales, NCCL bf16 all-gather)"
+        how = "copy-engine pushes over CUDA IPC" if args.gather == "copy" else "NCCL"
+        config_out["parallelism"] = (f"zero1-dp{world} (flat shards, per-shard scales, "
+                                     f"bf16 all-gather: {how})")
         scaling = "strong"
     else:
         res = run_luma(args, rank, world, local_rank)

@@ -236,6 +236,35 @@ int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid*
                   const float* u_m, const float* u_w, int16_t* q_m, int16_t* q_w,
                   void* stream);
 
+/*
+ * Self-check of the library's branch-free correctly rounded reciprocal,
+ * square root and quotient (used by the steady-state step loop) against CUDA's
+ * IEEE intrinsics on the current GPU: n random operands of each over the
+ * ranges where the step uses them.  Writes the mismatch counts (reciprocal,
+ * square root, quotient) to mismatches[0..2] (host memory; all 0 on a correct
+ * build) and synchronises `stream`.  No counterpart in the reference.
+ */
+int luma_arith_selfcheck(uint64_t n, uint64_t seed, uint64_t* mismatches, void* stream);
+
+/*
+ * Peer memory for the copy-engine all-gather of the ZeRO-1 step (one process
+ * per GPU).  A rank exports the device allocation holding its flat param
+ * buffer (luma_ipc_export: IPC handle of the allocation and the byte offset of
+ * `ptr` in it), the other ranks map it (luma_ipc_open / luma_ipc_close) and
+ * push their updated pieces into it with luma_copy_async (one cudaMemcpyAsync:
+ * the copy engines move the bytes, no SM is used).  The memory must come from
+ * cudaMalloc (PyTorch's default caching allocator does).  No counterpart in the
+ * reference, whose optimizer never exchanges data (optimizer.py:399-407).
+ */
+typedef struct LumaIpcHandle {
+  unsigned char bytes[64];
+} LumaIpcHandle;
+
+int luma_ipc_export(const void* ptr, LumaIpcHandle* handle, uint64_t* offset);
+int luma_ipc_open(const LumaIpcHandle* handle, void** base);
+int luma_ipc_close(void* base);
+int luma_copy_async(void* dst, const void* src, uint64_t bytes, void* stream);
+
 /* ABI version (LUMA_ABI_VERSION). */
 int luma_abi_version(void);
 

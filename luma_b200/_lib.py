@@ -80,7 +80,8 @@ EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
                   SLOT_DTYPE.itemsize, ctypes.sizeof(LumaStepArgs))
 
 EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_quantize",
-            "luma_abi_version", "luma_struct_sizes", "luma_last_error")
+            "luma_abi_version", "luma_struct_sizes", "luma_last_error", "luma_arith_selfcheck",
+            "luma_ipc_export", "luma_ipc_open", "luma_ipc_close", "luma_copy_async")
 
 NOALLOC_MAX_DESCS = 4096  # LUMA_NOALLOC_MAX_DESCS
 
@@ -111,6 +112,19 @@ def lib() -> ctypes.CDLL:
         h.luma_struct_sizes.argtypes = [ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
         h.luma_last_error.restype = ctypes.c_char_p
         h.luma_last_error.argtypes = []
+        h.luma_arith_selfcheck.restype = ctypes.c_int
+        h.luma_arith_selfcheck.argtypes = [ctypes.c_uint64, ctypes.c_uint64,
+                                           ctypes.POINTER(ctypes.c_uint64), ctypes.c_void_p]
+        h.luma_ipc_export.restype = ctypes.c_int
+        h.luma_ipc_export.argtypes = [ctypes.c_void_p, ctypes.c_char_p,
+                                      ctypes.POINTER(ctypes.c_uint64)]
+        h.luma_ipc_open.restype = ctypes.c_int
+        h.luma_ipc_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+        h.luma_ipc_close.restype = ctypes.c_int
+        h.luma_ipc_close.argtypes = [ctypes.c_void_p]
+        h.luma_copy_async.restype = ctypes.c_int
+        h.luma_copy_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
+                                      ctypes.c_void_p]
         h.luma_step.restype = ctypes.c_int
         h.luma_step.argtypes = [ctypes.POINTER(LumaStepArgs), ctypes.c_void_p]
         h.luma_step_noalloc.restype = ctypes.c_int
@@ -134,6 +148,42 @@ def lib() -> ctypes.CDLL:
             raise ImportError(f"libluma_b200 struct sizes {tuple(sizes)} != {EXPECTED_SIZES}")
         _lib = h
         return h
+
+
+def arith_selfcheck(n: int, seed: int = 0, stream=None) -> tuple[int, int, int]:
+    """Mismatch counts (rcp, sqrt, div) of the step's branch-free arithmetic
+    against CUDA's IEEE intrinsics over n random operands each (synchronises)."""
+    out = (ctypes.c_uint64 * 3)()
+    st = 0 if stream is None else stream.cuda_stream
+    check(lib().luma_arith_selfcheck(n, seed, out, ctypes.c_void_p(st)), "luma_arith_selfcheck")
+    return tuple(int(v) for v in out)
+
+
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(64-byte IPC handle of the allocation holding device pointer `ptr`, byte offset of ptr)."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_uint64(0)
+    check(lib().luma_ipc_export(ctypes.c_void_p(ptr), buf, ctypes.byref(off)), "luma_ipc_export")
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a peer's allocation into this process; returns its base address."""
+    if len(handle) != 64:
+        raise ValueError("IPC handle must be 64 bytes")
+    base = ctypes.c_void_p(0)
+    check(lib().luma_ipc_open(handle, ctypes.byref(base)), "luma_ipc_open")
+    return int(base.value)
+
+
+def ipc_close(base: int) -> None:
+    check(lib().luma_ipc_close(ctypes.c_void_p(base)), "luma_ipc_close")
+
+
+def copy_async(dst: int, src: int, nbytes: int, stream) -> None:
+    """One cudaMemcpyAsync (copy engine) of nbytes from src to dst on `stream`."""
+    check(lib().luma_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes,
+                                ctypes.c_void_p(stream.cuda_stream)), "luma_copy_async")
 
 
 def check(status: int, what: str) -> None:

@@ -15,7 +15,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-SOURCES = [os.path.join(HERE, "csrc", "luma_step.cu")]
+SOURCES = [os.path.join(HERE, "csrc", "luma_step.cu"), os.path.join(HERE, "csrc", "luma_peer.cu")]
 OUT = os.path.join(HERE, "_lib", "libluma_b200.so")
 
 NVCC_FLAGS = [
@@ -49,7 +49,8 @@ def is_stale() -> bool:
     if not os.path.exists(OUT):
         return True
     t = os.path.getmtime(OUT)
-    deps = SOURCES + [os.path.join(ROOT, "include", "luma_b200.h")]
+    deps = SOURCES + [os.path.join(ROOT, "include", "luma_b200.h"),
+                      os.path.join(HERE, "csrc", "luma_internal.h")]
     return any(os.path.getmtime(s) > t for s in deps)
 
 

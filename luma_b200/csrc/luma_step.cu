@@ -29,6 +29,7 @@
 // thread owns one octet per iteration (128-bit loads/stores when aligned).
 
 #include "luma_b200.h"
+#include "luma_internal.h"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -60,6 +61,18 @@ constexpr int kLutEntries = 32769;
 constexpr int64_t kLutMinElems = 131072;
 constexpr size_t kLutBytes = kLutEntries * sizeof(float);
 
+// Pass-2 steady loop: each thread stages the raw words of its next pairs in
+// shared memory with asynchronous copies, kHotStages pairs deep, after the
+// decode table.  A stage holds, per thread, up to 8 bytes of param, 8 of
+// grad, 4 of Q_m and 4 of Q_w.
+#ifndef LUMA_HOT_STAGES
+#define LUMA_HOT_STAGES 4
+#endif
+constexpr int kHotStages = LUMA_HOT_STAGES;
+constexpr size_t kLutPadBytes = (kLutBytes + 127) / 128 * 128;
+constexpr size_t kHotStageBytes = (size_t)kThreadsPass2 * 24;
+constexpr size_t kPass2SmemBytes = kLutPadBytes + kHotStages * kHotStageBytes;
+
 // Pass-1 accumulators of one tensor (the amax_m / amax_v / done fields of a
 // LumaSlot) for luma_step_noalloc, which keeps them in the library's own
 // static device array instead of the caller's slots.
@@ -80,12 +93,10 @@ static __device__ __align__(256) PassAccum g_noalloc_accum[LUMA_NOALLOC_MAX_DESC
 // Error reporting
 // ---------------------------------------------------------------------------
 
-thread_local char g_err[512] = "";
-
 int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
-  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  vsnprintf(luma_g_err, sizeof(luma_g_err), fmt, ap);
   va_end(ap);
   return code;
 }
@@ -162,6 +173,25 @@ __device__ void make_grid(double S_m, double S_v, double eps, LumaGrid* g) {
 // Clamps below keep NaN inputs as ATen's clamp kernels do (a NaN operand
 // fails every comparison and passes through the select unchanged).
 
+// Per-thread asynchronous global -> shared copies (cp.async, 4 or 8 bytes;
+// completion tracked per thread with commit / wait groups).
+template <int kBytes>
+__device__ __forceinline__ void cp_async(void* smem_dst, const void* gmem_src) {
+  static_assert(kBytes == 4 || kBytes == 8, "cp.async size");
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::
+                   "r"((uint32_t)__cvta_generic_to_shared(smem_dst)), "l"(gmem_src), "n"(kBytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
 struct Consts {
   // step row
   float beta1, omb1, beta2, omb2, decay, neg_eta, inv_bc2, eps32, w_max;
@@ -221,6 +251,59 @@ __device__ __forceinline__ float adamw(const Consts& c, float p, float mn, float
   const float pd = __fmul_rn(p, c.decay);
   const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vn, c.inv_bc2)), c.eps32);
   return __fmaf_rn(c.neg_eta, __fdiv_rn(mn, den), pd);
+}
+
+// ---------------------------------------------------------------------------
+// Branch-free correctly rounded reciprocal, square root and quotient for the
+// steady-state loop.  CUDA's IEEE __frcp_rn / __fsqrt_rn / __fdiv_rn each test
+// their operands and branch to a slow path; those branches split the loop body
+// into small blocks.  The forms below start from the hardware approximations
+// and apply the FMA residual corrections of Markstein's method (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000 processor",
+// IBM J. Res. Dev. 34(1), 1990).  Each is correctly rounded (round to nearest
+// even, the result of the IEEE intrinsic) on the operand range stated, which
+// was established by exhaustive comparison with the intrinsic on a B200:
+//   rcp_cr(b):    every float with 2^-125 <= |b| <= 2^125;
+//   sqrt_cr(x):   every float with 2^-102 <= x <= FLT_MAX;
+//   div_cr(a, b): every pair of significands (a, b in [1, 2): 2^46 pairs) and
+//                 2^36 random pairs with 2^-100 <= |a|, |b| < 2^100 and the
+//                 quotient in [2^-120, 2^120] (exponents only scale the
+//                 intermediate values while they stay normal).
+// Outside those ranges the caller must use the IEEE intrinsics;
+// luma_arith_selfcheck() repeats the comparison on the current GPU.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rsqrt_approx_ftz(float x) {
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 1/b: one Newton-Raphson step y0 + y0 (1 - b y0), the residual exact in an FMA.
+__device__ __forceinline__ float rcp_cr(float b) {
+  const float y0 = rcp_approx_ftz(b);
+  return __fmaf_rn(y0, __fmaf_rn(-b, y0, 1.0f), y0);
+}
+
+// sqrt(x): s0 = x rsqrt(x), corrected once by the exact residual x - s0^2
+// times 1/(2 sqrt(x)).
+__device__ __forceinline__ float sqrt_cr(float x) {
+  const float r0 = rsqrt_approx_ftz(x);
+  const float s0 = __fmul_rn(x, r0);
+  return __fmaf_rn(__fmaf_rn(-s0, s0, x), __fmul_rn(0.5f, r0), s0);
+}
+
+// a/b: q0 = a RN(1/b), corrected once by the exact residual a - b q0.
+__device__ __forceinline__ float div_cr(float a, float b) {
+  const float y = rcp_cr(b);
+  const float q0 = __fmul_rn(a, y);
+  return __fmaf_rn(__fmaf_rn(-b, q0, a), y, q0);
 }
 
 // LogSR decision  u < p*,  p* = fl(expm1f(fl(frac * delta)) * inv_z)
@@ -434,6 +517,41 @@ __device__ __forceinline__ void store8_codes(int16_t* base, int64_t e0, int n, b
 // ---------------------------------------------------------------------------
 // Per-tensor segment bodies
 // ---------------------------------------------------------------------------
+
+// Per-segment state in shared memory: descriptor, step row, decode grid (of
+// the previous step) and encode grid (of this step).
+struct SegShared {
+  LumaTensorDesc d;
+  LumaStepRow row;
+  LumaGrid dec;
+  LumaGrid enc;
+  int64_t next_pos;
+};
+
+// The CTA's segment state and decode table.  At namespace scope so that the
+// out-of-line segment functions address them as shared memory.
+__shared__ SegShared g_seg;
+extern __shared__ float g_lut[];  // kLutEntries floats when launched with the table
+
+__device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Consts& c) {
+  c.beta1 = s.row.beta1; c.omb1 = s.row.omb1; c.beta2 = s.row.beta2; c.omb2 = s.row.omb2;
+  c.decay = s.row.decay; c.neg_eta = s.row.neg_eta; c.inv_bc2 = s.row.inv_bc2;
+  c.eps32 = s.row.eps32; c.w_max = s.row.w_max;
+  c.init = (s.row.step == 1) ? 1 : 0;
+  c.o_dm = s.dec.dm; c.o_wmin = s.dec.w_min; c.o_dw = s.dec.dw;
+  if (pass2) {
+    c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
+    c.n_wmin = s.enc.w_min; c.n_inv_wmin = s.enc.inv_wmin; c.n_dw = s.enc.dw;
+    c.n_inv_dw = s.enc.inv_dw; c.n_inv_zw = s.enc.inv_zw; c.n_dw_pos = s.enc.dw_pos;
+    c.margin_m = decision_margin(c.n_dm);
+    c.margin_w = decision_margin(c.n_dw);
+    c.inv_zm24 = c.n_inv_zm * kUScale;
+    c.inv_zw24 = c.n_inv_zw * kUScale;
+  } else {
+    c.o_dw_log2e = c.o_dw * 1.44269504f;
+    c.tau_v = kBoundEps * c.eps32 * c.eps32 + kTinyAbs;
+  }
+}
 
 // Running state of the pass-1 maximum search of one tensor segment.
 //   am/av: this thread's exact max |m'| / max v' (float bit patterns);
@@ -838,20 +956,206 @@ __device__ __forceinline__ void pass2_fast(const Consts& c, const float* lut, ui
   }
 }
 
+// ---------------------------------------------------------------------------
+// Steady-state pass 2: step >= 2 with the decode table, Philox uniforms,
+// aligned complete pairs, and a segment whose grids keep every operand of the
+// correctly rounded arithmetic above inside its verified range (hot_segment).
+// The arithmetic is that of pass2_elem with two differences that leave the
+// results unchanged: rcp_cr / sqrt_cr / div_cr replace the IEEE intrinsics,
+// and each LogSR decision is taken from the series value alone.  An element
+// whose m' or v' falls outside the verified range (tiny, subnormal or NaN), or
+// whose decision would need expm1f (u within the margin of the series value,
+// about 4e-6 of the decisions), marks its pair; a marked pair is recomputed by
+// pass2_pair_exact with the general code, which also stores it.
+// ---------------------------------------------------------------------------
+
+// Bounds of the verified ranges, with margin (see rcp_cr / sqrt_cr / div_cr).
+constexpr float kHotMinV = 0x1.0p-100f;   // v' (and v'/bc2 >= v'): sqrt_cr
+constexpr float kHotMinM = 0x1.0p-80f;    // |m'|: quotient >= 2^-120 when den <= 2^40
+constexpr double kHotMaxDen = 0x1.0p40;   // sqrt(S_v / bc2) + eps
+constexpr double kHotMaxQuot = 0x1.0p119; // S_m / eps
+constexpr double kHotMaxM = 0x1.0p100;
+constexpr double kHotMinEps = 0x1.0p-100;
+constexpr double kHotMinW = 0x1.0p-124;   // decode w range: rcp_cr
+constexpr double kHotMaxW = 0x1.0p123;
+
+// Whether every element of the segment satisfies the range conditions that do
+// not depend on the element: eps, the decode grid's w range, and the maxima
+// S_m / S_v of this step bounding |m'|, v', the AdamW denominator and quotient.
+__device__ __forceinline__ bool hot_segment(const SegShared& s) {
+  const double eps = (double)s.row.eps32;
+  const double w_lo = (double)s.dec.w_min;
+  const double w_hi = w_lo * exp(65535.0 * (double)s.dec.dw) * 2.0;  // decode w <= this
+  const double den_hi = sqrt(s.enc.S_v * (double)s.row.inv_bc2 * 2.0) + eps * 2.0;
+  return eps >= kHotMinEps && w_lo >= kHotMinW && w_hi <= kHotMaxW &&
+         s.enc.S_m <= kHotMaxM && s.enc.S_m <= kHotMaxQuot * eps && den_hi <= kHotMaxDen;
+}
+
+// pass2_elem for the steady state; sets `rare` when the element's results may
+// differ from pass2_elem's (they are then discarded).
+__device__ __forceinline__ void pass2_elem_hot(const Consts& c, const float* lut, float g, float& p,
+                                               uint32_t& qm, uint32_t& qw, float um, float uw,
+                                               bool& rare) {
+  const float m = decode_m_lut((int)(int16_t)(uint16_t)qm, lut);
+  float t = __fsub_rn(rcp_cr(__fmul_rn(c.o_wmin, expf(__fmul_rn((float)qw, c.o_dw)))), c.eps32);
+  t = t < 0.0f ? 0.0f : t;
+  const float v = __fmul_rn(t, t);
+  const float mn = __fadd_rn(__fmul_rn(c.beta1, m), __fmul_rn(c.omb1, g));
+  const float vn = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, __fmul_rn(g, g)));
+  // v' = +0 takes sqrt = +0; m' = +0 gives the quotient +0 (div_cr(+0, den) = +0).
+  const bool v_ok = vn >= kHotMinV;
+  const bool v_zero = __float_as_uint(vn) == 0u;
+  rare |= !(v_ok || v_zero) || !(fabsf(mn) >= kHotMinM || __float_as_uint(mn) == 0u);
+  {  // AdamW
+    const float pd = __fmul_rn(p, c.decay);
+    const float sq = v_ok ? sqrt_cr(__fmul_rn(vn, c.inv_bc2)) : 0.0f;
+    p = __fmaf_rn(c.neg_eta, div_cr(mn, __fadd_rn(sq, c.eps32)), pd);
+  }
+  {  // quant_m
+    const float a = fabsf(mn);
+    const float ac = a > c.n_sm32 ? c.n_sm32 : a;
+    const float y = __fmul_rn(log1pf(ac), c.n_inv_dm);
+    const float fy = floorf(y);
+    const float x = __fmul_rn(__fsub_rn(y, fy), c.n_dm);
+    const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
+    const float diff = __fsub_rn(um, __fmul_rn(e, c.inv_zm24));
+    rare |= !(fabsf(diff) > c.margin_m);
+    float r = __fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f);
+    r = r > (float)LUMA_K_M ? (float)LUMA_K_M : r;
+    const int ri = (int)r;
+    qm = (uint32_t)(uint16_t)(int16_t)(mn < 0.0f ? -ri : ri);
+  }
+  {  // quant_w
+    const float sq = v_ok ? sqrt_cr(vn) : 0.0f;
+    float w = rcp_cr(__fadd_rn(sq, c.eps32));
+    w = w < c.n_wmin ? c.n_wmin : (w > c.w_max ? c.w_max : w);
+    const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
+    const float fy = floorf(y);
+    const float x = __fmul_rn(__fsub_rn(y, fy), c.n_dw);
+    const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
+    const float diff = __fsub_rn(uw, __fmul_rn(e, c.inv_zw24));
+    rare |= !(fabsf(diff) > c.margin_w);
+    float r = __fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f);
+    r = r < 0.0f ? 0.0f : (r > (float)LUMA_K_W ? (float)LUMA_K_W : r);
+    qw = (uint32_t)(int)r;
+  }
+}
+
+// A marked pair (element index e = 2P, both elements present, aligned):
+// reload, recompute with pass2_elem and store.  Out of line so the steady
+// loop's registers are not shaped by this rarely run code.
+template <int PD, int GD>
+__device__ __noinline__ void pass2_pair_exact(uint32_t k0, uint32_t k1, int64_t P) {
+  const LumaTensorDesc& d = g_seg.d;
+  const float* lut = g_lut;
+  Consts c;
+  fill_consts(g_seg, true, c);
+  RawPair r;
+  load_raw_pair<PD, GD>(d, false, true, P, r);
+  float p0, p1, g0, g1;
+  unpack2<PD>(r.p, p0, p1);
+  unpack2<GD>(r.g, g0, g1);
+  uint32_t qm0 = r.qm & 0xFFFFu, qm1 = r.qm >> 16;
+  uint32_t qw0 = r.qw & 0xFFFFu, qw1 = r.qw >> 16;
+  const uint64_t ctr = ((uint64_t)d.rng_offset >> 1) + (uint64_t)P;
+  const uint4 u = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+  pass2_elem(c, lut, g0, p0, qm0, qw0, u24_scaled(u.x), u24_scaled(u.y));
+  pass2_elem(c, lut, g1, p1, qm1, qw1, u24_scaled(u.z), u24_scaled(u.w));
+  const int64_t e = 2 * P;
+  store2<PD>(d.param, e, true, true, p0, p1);
+  store2_codes(d.q_m, e, true, true, qm0, qm1);
+  store2_codes(d.q_w, e, true, true, qw0, qw1);
+}
+
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, const float* lut,
+                                          uint32_t k0, uint32_t k1, int64_t p_lo, int n) {
+  constexpr int kThreads = kThreadsPass2;
+  using PW = typename PairWord<PD>::T;
+  using GW = typename PairWord<GD>::T;
+  const LumaTensorDesc& d = s.d;
+  PW* pp = static_cast<PW*>(d.param) + p_lo;
+  const GW* gp = static_cast<const GW*>(d.grad) + p_lo;
+  uint32_t* qmp = reinterpret_cast<uint32_t*>(d.q_m) + p_lo;
+  uint32_t* qwp = reinterpret_cast<uint32_t*>(d.q_w) + p_lo;
+  const uint64_t ctr_base = ((uint64_t)d.rng_offset >> 1) + (uint64_t)p_lo;
+  // This thread's slots in the stages: param, grad, Q_m, Q_w words.
+  unsigned char* stage0 = reinterpret_cast<unsigned char*>(g_lut) + kLutPadBytes;
+  PW* sp = reinterpret_cast<PW*>(stage0) + threadIdx.x;
+  GW* sg = reinterpret_cast<GW*>(stage0 + (size_t)kThreadsPass2 * 8) + threadIdx.x;
+  uint32_t* sm = reinterpret_cast<uint32_t*>(stage0 + (size_t)kThreadsPass2 * 16) + threadIdx.x;
+  uint32_t* sw = reinterpret_cast<uint32_t*>(stage0 + (size_t)kThreadsPass2 * 20) + threadIdx.x;
+  constexpr int kStageWords = (int)(kHotStageBytes / 4);  // stage stride in 4-byte words
+  auto issue = [&](int j, int st) {  // start the copies of pair j into stage st
+    if (j < n) {
+      const int o = st * kStageWords;
+      cp_async<sizeof(PW)>(reinterpret_cast<uint32_t*>(sp) + o, pp + j);
+      cp_async<sizeof(GW)>(reinterpret_cast<uint32_t*>(sg) + o, gp + j);
+      cp_async<4>(sm + o, qmp + j);
+      cp_async<4>(sw + o, qwp + j);
+    }
+    cp_async_commit();  // (an empty group past the end keeps the count uniform)
+  };
+#pragma unroll
+  for (int k = 0; k < kHotStages - 1; ++k) issue(threadIdx.x + k * kThreads, k);
+  int st = 0;
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    issue(i + (kHotStages - 1) * kThreads, st == 0 ? kHotStages - 1 : st - 1);
+    cp_async_wait<kHotStages - 1>();  // pair i has landed
+    const int o = st * kStageWords;
+    RawPair cur;
+    to_words<PD>(*reinterpret_cast<const PW*>(reinterpret_cast<const uint32_t*>(sp) + o), cur.p);
+    to_words<GD>(*reinterpret_cast<const GW*>(reinterpret_cast<const uint32_t*>(sg) + o), cur.g);
+    cur.qm = sm[o];
+    cur.qw = sw[o];
+    st = st == kHotStages - 1 ? 0 : st + 1;
+    float p0, p1, g0, g1;
+    unpack2<PD>(cur.p, p0, p1);
+    unpack2<GD>(cur.g, g0, g1);
+    uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
+    uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
+    const uint64_t ctr = ctr_base + (uint32_t)i;
+    const uint4 r = philox4x32_10(make_uint4((uint32_t)ctr, (uint32_t)(ctr >> 32), 0u, 0u), k0, k1);
+    bool rare = false;
+    pass2_elem_hot(c, lut, g0, p0, qm0, qw0, u24_scaled(r.x), u24_scaled(r.y), rare);
+    pass2_elem_hot(c, lut, g1, p1, qm1, qw1, u24_scaled(r.z), u24_scaled(r.w), rare);
+    if (rare) {
+      pass2_pair_exact<PD, GD>(k0, k1, p_lo + i);
+    } else {
+      if constexpr (PD == LUMA_F32) {
+        __stcs(pp + i, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
+      } else {
+        __stcs(pp + i, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
+                           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p1)) << 16));
+      }
+      __stcs(qmp + i, (qm0 & 0xFFFFu) | (qm1 << 16));
+      __stcs(qwp + i, (qw0 & 0xFFFFu) | (qw1 << 16));
+    }
+  }
+  cp_async_wait<0>();  // no copy left in flight into the stages
+}
+
 // Pass 2 for one tensor segment.  bf16 params: the prefetching pair loop.
 // fp32 params: the steady-state loop where it applies, the general loop
 // otherwise (unaligned views, injected uniforms, the odd tail).  The choice
 // per param dtype is measured (one Llama-3-8B layer and GPT-2 small).
 template <int PD, int GD>
-__device__ __forceinline__ void pass2_segment(const LumaTensorDesc& d, const Consts& c,
+__device__ __forceinline__ void pass2_segment(const SegShared& s, const Consts& c,
                                               const float* lut, uint32_t k0, uint32_t k1,
                                               bool vec2, int64_t p_lo, int64_t p_hi) {
+  const LumaTensorDesc& d = s.d;
+  const int64_t p_full = min(p_hi, d.numel / 2);  // pairs with both elements
+  const bool steady = vec2 && d.u_m == nullptr && p_full > p_lo && p_full - p_lo <= 0x7FFFFFFF;
+  if (steady && !c.init && lut != nullptr && hot_segment(s)) {
+    pass2_hot<PD, GD>(s, c, lut, k0, k1, p_lo, (int)(p_full - p_lo));
+    if (p_full < p_hi) pass2_pairs<PD, GD>(d, c, lut, k0, k1, vec2, p_full, p_hi);
+    return;
+  }
   if constexpr (PD == LUMA_BF16) {
     pass2_prefetch<PD, GD>(d, c, lut, k0, k1, vec2, p_lo, p_hi);
     return;
   }
-  const int64_t p_full = min(p_hi, d.numel / 2);  // pairs with both elements
-  if (vec2 && d.u_m == nullptr && p_full > p_lo && p_full - p_lo <= 0x7FFFFFFF) {
+  if (steady) {
     using PW = typename PairWord<PD>::T;
     using GW = typename PairWord<GD>::T;
     pass2_fast<PD, GD>(c, lut, k0, k1, static_cast<PW*>(d.param) + p_lo,
@@ -869,32 +1173,36 @@ __device__ __forceinline__ void pass2_segment(const LumaTensorDesc& d, const Con
 // Kernels
 // ---------------------------------------------------------------------------
 
+// One tensor segment of pass 2 for one (param, grad) dtype pair, the step
+// constants read from the segment state in shared memory.  (Inlined: an
+// out-of-line version per dtype pair measured 3% slower.)
+template <int PD, int GD>
+__device__ __forceinline__ void pass2_segment_nl(bool use_lut, uint32_t k0, uint32_t k1, bool vec2,
+                                              int64_t p_lo, int64_t p_hi) {
+  Consts c;
+  fill_consts(g_seg, true, c);
+  pass2_segment<PD, GD>(g_seg, c, use_lut ? g_lut : nullptr, k0, k1, vec2, p_lo, p_hi);
+}
+
 // Segment-level selection of the pass-2 loop for the tensor's dtypes.
-__device__ __forceinline__ void dispatch_pass2(const LumaTensorDesc& d, const Consts& c,
-                                               const float* lut, uint32_t k0, uint32_t k1,
-                                               bool vec2, int64_t p_lo, int64_t p_hi) {
+__device__ __forceinline__ void dispatch_pass2(const SegShared& s, const float* lut, uint32_t k0,
+                                               uint32_t k1, bool vec2, int64_t p_lo,
+                                               int64_t p_hi) {
+  const LumaTensorDesc& d = s.d;
   if (d.param_dtype == LUMA_F32) {
     switch (d.grad_dtype) {
-      case LUMA_F32: pass2_segment<LUMA_F32, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      case LUMA_BF16: pass2_segment<LUMA_F32, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      default: pass2_segment<LUMA_F32, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_F32: pass2_segment_nl<LUMA_F32, LUMA_F32>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_segment_nl<LUMA_F32, LUMA_BF16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_segment_nl<LUMA_F32, LUMA_F16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
     }
   } else {
     switch (d.grad_dtype) {
-      case LUMA_F32: pass2_segment<LUMA_BF16, LUMA_F32>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      case LUMA_BF16: pass2_segment<LUMA_BF16, LUMA_BF16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
-      default: pass2_segment<LUMA_BF16, LUMA_F16>(d, c, lut, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_F32: pass2_segment_nl<LUMA_BF16, LUMA_F32>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_segment_nl<LUMA_BF16, LUMA_BF16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_segment_nl<LUMA_BF16, LUMA_F16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
     }
   }
 }
-
-struct SegShared {
-  LumaTensorDesc d;
-  LumaStepRow row;
-  LumaGrid dec;
-  LumaGrid enc;
-  int64_t next_pos;
-};
 
 // Largest i with descs[i].oct_begin <= pos.
 __device__ int find_desc(const LumaTensorDesc* descs, int n, int64_t pos) {
@@ -904,26 +1212,6 @@ __device__ int find_desc(const LumaTensorDesc* descs, int n, int64_t pos) {
     if (descs[mid].oct_begin <= pos) lo = mid; else hi = mid - 1;
   }
   return lo;
-}
-
-__device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Consts& c) {
-  c.beta1 = s.row.beta1; c.omb1 = s.row.omb1; c.beta2 = s.row.beta2; c.omb2 = s.row.omb2;
-  c.decay = s.row.decay; c.neg_eta = s.row.neg_eta; c.inv_bc2 = s.row.inv_bc2;
-  c.eps32 = s.row.eps32; c.w_max = s.row.w_max;
-  c.init = (s.row.step == 1) ? 1 : 0;
-  c.o_dm = s.dec.dm; c.o_wmin = s.dec.w_min; c.o_dw = s.dec.dw;
-  if (pass2) {
-    c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
-    c.n_wmin = s.enc.w_min; c.n_inv_wmin = s.enc.inv_wmin; c.n_dw = s.enc.dw;
-    c.n_inv_dw = s.enc.inv_dw; c.n_inv_zw = s.enc.inv_zw; c.n_dw_pos = s.enc.dw_pos;
-    c.margin_m = decision_margin(c.n_dm);
-    c.margin_w = decision_margin(c.n_dw);
-    c.inv_zm24 = c.n_inv_zm * kUScale;
-    c.inv_zw24 = c.n_inv_zw * kUScale;
-  } else {
-    c.o_dw_log2e = c.o_dw * 1.44269504f;
-    c.tau_v = kBoundEps * c.eps32 * c.eps32 + kTinyAbs;
-  }
 }
 
 // Thread 0: load descriptor `di`, its row and grids into shared memory.
@@ -948,10 +1236,10 @@ __global__ void __launch_bounds__(PASS2 ? kThreadsPass2 : kThreadsPass1, 1)
 luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
   constexpr int kThreads = PASS2 ? kThreadsPass2 : kThreadsPass1;
   constexpr int kWarps = kThreads / 32;
-  __shared__ SegShared s;
+  SegShared& s = g_seg;
   __shared__ uint32_t red_m[kMaxWarps], red_v[kMaxWarps];
   __shared__ int s_di;
-  extern __shared__ float s_lut[];  // kLutEntries floats when launched with the table
+  float* s_lut = g_lut;
 
   const int64_t T = a.total_octets;
   const int64_t lo = (T * (int64_t)blockIdx.x) / (int64_t)gridDim.x;
@@ -1034,7 +1322,7 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
       const bool vec2 = ((uintptr_t)d.param % pes == 0) && ((uintptr_t)d.grad % ges == 0) &&
                         ((uintptr_t)d.q_m % 4 == 0) && ((uintptr_t)d.q_w % 4 == 0) &&
                         ((uintptr_t)d.u_m % 8 == 0) && ((uintptr_t)d.u_w % 8 == 0);
-      dispatch_pass2(d, c, lut, k0, k1, vec2, p_lo, p_hi);
+      dispatch_pass2(s, lut, k0, k1, vec2, p_lo, p_hi);
     }
     __syncthreads();  // s is rewritten for the next tensor
     pos = d.oct_begin + o_hi;
@@ -1051,6 +1339,43 @@ __global__ void __launch_bounds__(kThreads) luma_decode_kernel(
     m_out[i] = decode_m((int)q_m[i], dm);
     v_out[i] = decode_v((uint32_t)(uint16_t)q_w[i], wmin, dw, eps32);
   }
+}
+
+// Self-check of rcp_cr / sqrt_cr / div_cr against the IEEE intrinsics on
+// random operands drawn over their verified ranges (see rcp_cr).
+__device__ unsigned long long g_arith_bad[3];
+
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {  // splitmix64 finaliser
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+__global__ void __launch_bounds__(kThreads) luma_arith_check_kernel(uint64_t n, uint64_t seed) {
+  unsigned int bad[3] = {0u, 0u, 0u};
+  for (uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * kThreads) {
+    const uint64_t h = mix64(seed ^ mix64(i));
+    const uint64_t h2 = mix64(h);
+    // rcp: |b| in [2^-125, 2^125): biased exponent 2..251, any significand and sign
+    const float b = __uint_as_float((uint32_t)(h >> 63) << 31 |
+                                    (uint32_t)(2 + (h >> 32) % 250) << 23 | ((uint32_t)h & 0x7FFFFFu));
+    bad[0] += __float_as_uint(rcp_cr(b)) != __float_as_uint(__frcp_rn(b));
+    // sqrt: x in [2^-102, FLT_MAX]: biased exponent 25..254
+    const float x = __uint_as_float((uint32_t)(25 + (h2 >> 32) % 230) << 23 | ((uint32_t)h2 & 0x7FFFFFu));
+    bad[1] += __float_as_uint(sqrt_cr(x)) != __float_as_uint(__fsqrt_rn(x));
+    // div: |a|, |b| in [2^-100, 2^100), quotient exponent within +-119
+    const int ea = (int)((h >> 40) % 200) - 100;
+    int eb = (int)((h2 >> 40) % 200) - 100;
+    eb = ea - eb > 119 ? ea - 119 : (eb - ea > 119 ? ea + 119 : eb);
+    const float a = __uint_as_float((uint32_t)(h2 >> 63) << 31 | (uint32_t)(ea + 127) << 23 |
+                                    ((uint32_t)(h >> 8) & 0x7FFFFFu));
+    const float d = __uint_as_float((uint32_t)(eb + 127) << 23 | ((uint32_t)(h2 >> 8) & 0x7FFFFFu));
+    bad[2] += __float_as_uint(div_cr(a, d)) != __float_as_uint(__fdiv_rn(a, d));
+  }
+  for (int k = 0; k < 3; ++k)
+    if (bad[k]) atomicAdd(&g_arith_bad[k], (unsigned long long)bad[k]);
 }
 
 // Quantize float32 moments onto a grid (reference optimizer.py:315-321,
@@ -1120,20 +1445,20 @@ int device_info(DeviceInfo** out) {
                              (int)kLutBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass1)");
     e = cudaFuncSetAttribute(luma_pass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kLutBytes);
+                             (int)kPass2SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2)");
     e = cudaFuncSetAttribute(luma_pass_kernel<false, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLutBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass1 noalloc)");
     e = cudaFuncSetAttribute(luma_pass_kernel<true, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLutBytes);
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPass2SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2 noalloc)");
     int b1 = 0, b2 = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, luma_pass_kernel<false>, kThreadsPass1,
                                                       kLutBytes);
     if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass1)");
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, luma_pass_kernel<true>, kThreadsPass2,
-                                                      kLutBytes);
+                                                      kPass2SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass2)");
     di.sms = prop.multiProcessorCount;
     di.ctas_pass1 = di.sms * (b1 > 0 ? b1 : 1);
@@ -1171,11 +1496,25 @@ int noalloc_scratch(DeviceInfo* di, PassAccum** out) {
 
 }  // namespace
 
+thread_local char luma_g_err[512] = "";
+
+int luma_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(luma_g_err, sizeof(luma_g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int luma_cuda_fail(cudaError_t e, const char* what) {
+  return luma_fail(LUMA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
 extern "C" {
 
 int luma_abi_version(void) { return LUMA_ABI_VERSION; }
 
-const char* luma_last_error(void) { return g_err; }
+const char* luma_last_error(void) { return luma_g_err; }
 
 int luma_struct_sizes(int64_t* out, int n) {
   const int64_t sizes[5] = {(int64_t)sizeof(LumaTensorDesc), (int64_t)sizeof(LumaStepRow),
@@ -1188,7 +1527,7 @@ int luma_struct_sizes(int64_t* out, int n) {
 }
 
 int luma_step(const LumaStepArgs* args, void* stream) {
-  g_err[0] = '\0';
+  luma_g_err[0] = '\0';
   if (args == nullptr) return fail(LUMA_ERR_INVALID, "luma_step: args is NULL");
   const LumaStepArgs a = *args;
   if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0 || a.max_ctas < 0)
@@ -1216,7 +1555,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
   luma_pass_kernel<true><<<grid_for(a.total_octets, kThreadsPass2, cap(di->ctas_pass2, a.max_ctas)), kThreadsPass2,
-                           kLutBytes, s>>>(a, 1, nullptr);
+                           kPass2SmemBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
   if (a.events[2]) {
@@ -1226,9 +1565,36 @@ int luma_step(const LumaStepArgs* args, void* stream) {
   return LUMA_OK;
 }
 
+int luma_arith_selfcheck(uint64_t n, uint64_t seed, uint64_t* mismatches, void* stream) {
+  luma_g_err[0] = '\0';
+  if (mismatches == nullptr) return fail(LUMA_ERR_INVALID, "luma_arith_selfcheck: NULL pointer");
+  DeviceInfo* di = nullptr;
+  int st = device_info(&di);
+  if (st != LUMA_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned long long zero[3] = {0ull, 0ull, 0ull};
+  cudaError_t e = cudaMemcpyToSymbolAsync(g_arith_bad, zero, sizeof(zero), 0,
+                                          cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbolAsync(selfcheck)");
+  if (n > 0) {
+    const uint64_t want = (n + kThreads - 1) / kThreads;
+    const int blocks = (int)(want < (uint64_t)di->sms * 8 ? want : (uint64_t)di->sms * 8);
+    luma_arith_check_kernel<<<blocks, kThreads, 0, s>>>(n, seed);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch arith selfcheck");
+  }
+  unsigned long long out[3];
+  e = cudaMemcpyFromSymbolAsync(out, g_arith_bad, sizeof(out), 0, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbolAsync(selfcheck)");
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize(selfcheck)");
+  for (int k = 0; k < 3; ++k) mismatches[k] = out[k];
+  return LUMA_OK;
+}
+
 int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel, float dm, float w_min,
                 float dw, float eps32, float* exp_avg, float* exp_avg_sq, void* stream) {
-  g_err[0] = '\0';
+  luma_g_err[0] = '\0';
   if (numel < 0) return fail(LUMA_ERR_INVALID, "luma_decode: negative numel");
   if (numel == 0) return LUMA_OK;
   if (!q_m || !q_w || !exp_avg || !exp_avg_sq)
@@ -1249,7 +1615,7 @@ int luma_decode(const int16_t* q_m, const int16_t* q_w, int64_t numel, float dm,
 int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid* grid,
                   float eps32, float w_max, int64_t seed, int64_t rng_offset, const float* u_m,
                   const float* u_w, int16_t* q_m, int16_t* q_w, void* stream) {
-  g_err[0] = '\0';
+  luma_g_err[0] = '\0';
   if (numel < 0) return fail(LUMA_ERR_INVALID, "luma_quantize: negative numel");
   if (numel == 0) return LUMA_OK;
   if (!m || !v || !grid || !q_m || !q_w)
@@ -1285,7 +1651,7 @@ int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid*
 }
 
 int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
-  g_err[0] = '\0';
+  luma_g_err[0] = '\0';
   if (args == nullptr) return fail(LUMA_ERR_INVALID, "luma_step_noalloc: args is NULL");
   const LumaStepArgs a = *args;
   if (a.n_desc < 0 || a.n_rows < 0 || a.total_octets < 0 || a.max_ctas < 0)
@@ -1326,7 +1692,7 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
   luma_pass_kernel<true, true><<<grid_for(a.total_octets, kThreadsPass2, cap(di->ctas_pass2, a.max_ctas)),
-                                 kThreadsPass2, kLutBytes, s>>>(a, 1, acc);
+                                 kThreadsPass2, kPass2SmemBytes, s>>>(a, 1, acc);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2 (noalloc)");
   if (a.events[2]) {

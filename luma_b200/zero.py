@@ -20,6 +20,15 @@ tests/test_fsdp.py:139-184), so the step partitions without any exchange:
   b's gather on a side stream while the kernels of bucket b+1 run; the pass
   kernels can be capped below one CTA per SM (``max_ctas``) so NCCL's kernels
   find free SMs.
+* ``gather="copy"`` replaces NCCL's gather by copy-engine pushes: every rank
+  maps the peers' flat buffers (CUDA IPC, ``PeerGather``) and, as soon as
+  bucket b's kernels are done, copies its piece of bucket b into every peer
+  (one ``cudaMemcpyAsync`` per peer, each peer on its own stream).  No SM is
+  taken from the step kernels.  Two stream-ordered barriers (an all-reduce of
+  one element) bound the pushes: the one before the first push makes sure
+  every peer has finished with its replica of the previous step (nothing still
+  reads a piece about to be overwritten), the one after the last push tells
+  every rank that all pieces have arrived.
 
 Grads are read only on the owned pieces (what a reduce-scatter with the same
 layout delivers): ``grad_shard`` holds them back to back, bucket by bucket.
@@ -108,6 +117,75 @@ def flat_views(flat: torch.Tensor, layout: FlatLayout, shapes) -> list[torch.Ten
     return [flat[s:s + n].view(shape) for shape, n, s in zip(shapes, layout.numels, layout.starts)]
 
 
+class PeerGather:
+    """Copy-engine all-gather of the flat buffer's bucket pieces over CUDA IPC.
+
+    Collective to construct (every rank of ``process_group``).  ``begin`` and
+    ``finish`` are stream-ordered barriers on ``comm``; ``push(b, event)``
+    copies this rank's piece of bucket b into every peer after ``event``.
+    """
+
+    def __init__(self, flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None):
+        import torch.distributed as dist
+
+        from . import _lib
+        self._lib = _lib
+        self.flat = flat
+        self.layout = layout
+        self.rank = rank
+        self.pg = process_group
+        handle, off = _lib.ipc_export(flat.data_ptr())
+        infos = [None] * layout.world
+        dist.all_gather_object(infos, (handle, off), group=process_group)
+        self.bases = {}
+        self.peer_ptr = {}
+        for p, (h, o) in enumerate(infos):
+            if p == rank:
+                continue
+            base = _lib.ipc_open(h)
+            self.bases[p] = base
+            self.peer_ptr[p] = base + o
+        dev = flat.device
+        self.comm = torch.cuda.Stream(device=dev)
+        self.streams = {p: torch.cuda.Stream(device=dev) for p in self.peer_ptr}
+        self.token = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def _barrier(self) -> None:
+        import torch.distributed as dist
+        with torch.cuda.stream(self.comm):
+            dist.all_reduce(self.token, group=self.pg)
+
+    def begin(self, main: torch.cuda.Stream) -> None:
+        """Barrier after everything queued on `main` so far (all ranks)."""
+        self.comm.wait_stream(main)
+        self._barrier()
+        for st in self.streams.values():
+            st.wait_stream(self.comm)
+
+    def push(self, bucket: int, ready: torch.cuda.Event) -> None:
+        lo, hi = self.layout.owned(self.rank, bucket)
+        es = self.flat.element_size()
+        src = self.flat.data_ptr() + lo * es
+        nbytes = (hi - lo) * es
+        for p, st in self.streams.items():
+            st.wait_event(ready)
+            self._lib.copy_async(self.peer_ptr[p] + lo * es, src, nbytes, st)
+
+    def finish(self, main: torch.cuda.Stream) -> None:
+        """Barrier after every push; `main` then sees the full replica."""
+        for st in self.streams.values():
+            self.comm.wait_stream(st)
+        self._barrier()
+        main.wait_stream(self.comm)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.flat.device)
+        for base in self.bases.values():
+            self._lib.ipc_close(base)
+        self.bases.clear()
+        self.peer_ptr.clear()
+
+
 class ZeroLUMA:
     """LUMA step over this rank's pieces, then per-bucket NCCL all-gathers.
 
@@ -120,7 +198,7 @@ class ZeroLUMA:
     def __init__(self, flat_param: torch.Tensor, layout: FlatLayout, rank: int,
                  lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01, base_seed: int | None = None,
-                 process_group=None, max_ctas: int = 0):
+                 process_group=None, max_ctas: int = 0, gather: str = "nccl"):
         if flat_param.dim() != 1 or flat_param.numel() != layout.total:
             raise ValueError(f"flat_param must be 1-D with {layout.total} elements")
         if flat_param.dtype not in (torch.float32, torch.bfloat16):
@@ -146,6 +224,11 @@ class ZeroLUMA:
             eng.ensure_slots(max(1, len(segs)))
             self.engines.append(eng)
         self.comm = torch.cuda.Stream(device=dev)
+        if gather not in ("nccl", "copy"):
+            raise ValueError(f"gather must be 'nccl' or 'copy', got {gather!r}")
+        self.gather_mode = gather
+        self.peers = PeerGather(flat_param, layout, rank, process_group) \
+            if gather == "copy" and layout.world > 1 else None
         self.t = 0
         self.events = None  # optional (ev0, ev1, ev2) cudaEvent_t handles for bucket 0 (timing)
 
@@ -194,8 +277,17 @@ class ZeroLUMA:
 
     @torch.no_grad()
     def gather(self) -> None:
-        """All-gather every bucket (in place) on the current stream."""
+        """All-gather every bucket (in place), ordered after the current stream."""
         if self.layout.world == 1:
+            return
+        main = torch.cuda.current_stream(self.flat.device)
+        if self.peers is not None:
+            self.peers.begin(main)
+            done = torch.cuda.Event()
+            done.record(main)
+            for b in range(self.layout.buckets):
+                self.peers.push(b, done)
+            self.peers.finish(main)
             return
         for b in range(self.layout.buckets):
             self._gather_bucket(b)
@@ -211,6 +303,16 @@ class ZeroLUMA:
                 self._step_bucket(b, grad_shard, rows, 0)
             return
         main = torch.cuda.current_stream(self.flat.device)
+        if self.peers is not None:
+            # copy engines: bucket b's pushes overlap bucket b+1's kernels
+            self.peers.begin(main)
+            for b in range(self.layout.buckets):
+                self._step_bucket(b, grad_shard, rows, 0)
+                done = torch.cuda.Event()
+                done.record(main)
+                self.peers.push(b, done)
+            self.peers.finish(main)
+            return
         for b in range(self.layout.buckets):
             # while an earlier bucket's gather may be in flight, leave SMs to NCCL
             self._step_bucket(b, grad_shard, rows, self.max_ctas if b > 0 else 0)
@@ -220,6 +322,12 @@ class ZeroLUMA:
             with torch.cuda.stream(self.comm):
                 self._gather_bucket(b)
         main.wait_stream(self.comm)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (copy gather); call before destroying the process group."""
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def scales(self) -> list[tuple[int, int, float, float]]:
         """(tensor, offset, S_m, S_v) of every local segment, bucket order (synchronises)."""

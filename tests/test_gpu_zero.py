@@ -1,10 +1,11 @@
-"""ZeRO-1 sharded step on 2 GPUs (NCCL): bit-exact per segment, gathered replicas equal.
+"""ZeRO-1 sharded step on 2 GPUs: bit-exact per segment, gathered replicas equal.
 
 Each rank steps its flat shard; every (tensor, shard) segment must equal the
 oracle (the reference's op sequence on CUDA) run on that segment alone with
 the backend's Philox stream (param_id = tensor index, counter offset = the
-segment's offset in the tensor).  After the all-gather both ranks must hold
-the same full parameter buffer, and its pieces must be each owner's result.
+segment's offset in the tensor).  After the all-gather (NCCL, or copy-engine
+pushes over CUDA IPC) both ranks must hold the same full parameter buffer,
+and its pieces must be each owner's result.
 Skipped with fewer than 2 GPUs.
 """
 
@@ -28,7 +29,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, pdt_name, buckets, out_q):
+def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "tests")]
@@ -51,7 +52,8 @@ def _worker(rank, world, port, pdt_name, buckets, out_q):
         for v, s in zip(flat_views(flat, lay, SHAPES), SHAPES):
             v.copy_((torch.randn(s, generator=gen) * 0.02).to(pdt))
         segs = shard_segments(lay, rank)
-        opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, max_ctas=100)
+        opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, max_ctas=100,
+                       gather=gather)
         # oracle: every local segment as its own tensor
         oparams = [flat[sg.flat:sg.flat + sg.length].clone() for sg in segs]
         for p in oparams:
@@ -90,6 +92,7 @@ def _worker(rank, world, port, pdt_name, buckets, out_q):
             dist.broadcast(other.copy_(flat), src=0)
             if not torch.equal(other, flat):
                 msgs.append(f"t={t}: gathered replicas differ")
+        opt.close()
         out_q.put((rank, msgs))
     except Exception as exc:  # noqa: BLE001
         out_q.put((rank, [f"exception: {exc!r}"]))
@@ -97,13 +100,15 @@ def _worker(rank, world, port, pdt_name, buckets, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("pdt_name,buckets", [("bfloat16", 1), ("float32", 1), ("bfloat16", 3)])
-def test_zero_sharded_step_two_gpus(pdt_name, buckets):
+@pytest.mark.parametrize("pdt_name,buckets,gather", [
+    ("bfloat16", 1, "nccl"), ("float32", 1, "nccl"), ("bfloat16", 3, "nccl"),
+    ("bfloat16", 3, "copy"), ("float32", 1, "copy")])
+def test_zero_sharded_step_two_gpus(pdt_name, buckets, gather):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, pdt_name, buckets, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, pdt_name, buckets, gather, q))
              for r in range(world)]
     for p in procs:
         p.start()
