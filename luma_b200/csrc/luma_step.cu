@@ -19,9 +19,11 @@
 // scalar s is a multiply by fl32(1.0 / s), the reciprocal taken in float64;
 // addcdiv is one fma), so the
 // codes and params are bit-identical to the reference running on CUDA when
-// both consume the same uniforms.  No fast-math: expm1f, expf, log1pf, logf,
-// IEEE division and sqrt are the CUDA library's accurate versions, the same
-// functions PyTorch's element-wise kernels call.
+// both consume the same uniforms.  No fast-math: expm1f, expf, log1pf, logf
+// are the CUDA library's accurate versions, the same functions PyTorch's
+// element-wise kernels call; division, reciprocal and square root are the
+// IEEE intrinsics, or in the steady pass-2 loop branch-free correctly rounded
+// forms that equal them on the operand ranges where they are used.
 //
 // Work split: the flat space of all tensors, counted in octets (8 elements),
 // is cut into one contiguous range per CTA of a persistent grid sized from the
