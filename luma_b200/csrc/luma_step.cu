@@ -74,6 +74,14 @@ constexpr int kHotStages = LUMA_HOT_STAGES;
 constexpr size_t kLutPadBytes = (kLutBytes + 127) / 128 * 128;
 constexpr size_t kHotStageBytes = (size_t)kThreadsPass2 * 24;
 constexpr size_t kPass2SmemBytes = kLutPadBytes + kHotStages * kHotStageBytes;
+// Pass-1 staging (quantized steps of aligned tensors): per thread one quad
+// (4 elements) per stage: up to 16 bytes of grad, 8 of Q_m, 8 of Q_w.
+#ifndef LUMA_P1_STAGES
+#define LUMA_P1_STAGES 2
+#endif
+constexpr int kP1Stages = LUMA_P1_STAGES;
+constexpr size_t kP1StageBytes = (size_t)kThreadsPass1 * 32;
+constexpr size_t kPass1SmemBytes = kLutPadBytes + kP1Stages * kP1StageBytes;
 
 // Pass-1 accumulators of one tensor (the amax_m / amax_v / done fields of a
 // LumaSlot) for luma_step_noalloc, which keeps them in the library's own
@@ -179,10 +187,16 @@ __device__ void make_grid(double S_m, double S_v, double eps, LumaGrid* g) {
 // completion tracked per thread with commit / wait groups).
 template <int kBytes>
 __device__ __forceinline__ void cp_async(void* smem_dst, const void* gmem_src) {
-  static_assert(kBytes == 4 || kBytes == 8, "cp.async size");
-  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::
-                   "r"((uint32_t)__cvta_generic_to_shared(smem_dst)), "l"(gmem_src), "n"(kBytes)
-               : "memory");
+  static_assert(kBytes == 4 || kBytes == 8 || kBytes == 16, "cp.async size");
+  if constexpr (kBytes == 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::
+                     "r"((uint32_t)__cvta_generic_to_shared(smem_dst)), "l"(gmem_src)
+                 : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::
+                     "r"((uint32_t)__cvta_generic_to_shared(smem_dst)), "l"(gmem_src), "n"(kBytes)
+                 : "memory");
+  }
 }
 
 __device__ __forceinline__ void cp_async_commit() {
@@ -663,6 +677,71 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
     }
     ms.warp_sync_bounds();
   }
+}
+
+// Pass 1 over quads [q_lo, q_hi) (4 elements each, all complete) of an aligned
+// tensor at step >= 2: each thread copies the grad, Q_m and Q_w words of its
+// quad kP1Stages - 1 iterations ahead into its own shared-memory slots with
+// cp.async, so memory latency is hidden without holding the words in
+// registers.  All threads run the same number of iterations (warp reductions).
+template <int GD>
+__device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Consts& c,
+                                             const float* lut, int64_t q_lo, int64_t q_hi,
+                                             MaxSearch& ms) {
+  constexpr int kThreads = kThreadsPass1;
+  constexpr int kGB = GD == LUMA_F32 ? 16 : 8;  // grad bytes per quad
+  unsigned char* stage0 = reinterpret_cast<unsigned char*>(g_lut) + kLutPadBytes;
+  unsigned char* sg = stage0 + (size_t)threadIdx.x * 16;
+  unsigned char* sm = stage0 + (size_t)kThreads * 16 + (size_t)threadIdx.x * 8;
+  unsigned char* sw = stage0 + (size_t)kThreads * 24 + (size_t)threadIdx.x * 8;
+  const unsigned char* gq = static_cast<const unsigned char*>(d.grad) + q_lo * kGB;
+  const unsigned char* mq = reinterpret_cast<const unsigned char*>(d.q_m) + q_lo * 8;
+  const unsigned char* wq = reinterpret_cast<const unsigned char*>(d.q_w) + q_lo * 8;
+  const int64_t n = q_hi - q_lo;
+  auto issue = [&](int64_t j, int st) {  // quad j (relative) into stage st
+    if (j < n) {
+      const size_t o = (size_t)st * kP1StageBytes;
+      cp_async<kGB>(sg + o, gq + j * kGB);
+      cp_async<8>(sm + o, mq + j * 8);
+      cp_async<8>(sw + o, wq + j * 8);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int k = 0; k < kP1Stages - 1; ++k) issue(threadIdx.x + (int64_t)k * kThreads, k);
+  int st = 0;
+  for (int64_t jb = 0; jb < n; jb += kThreads) {
+    const int64_t j = jb + threadIdx.x;
+    issue(j + (int64_t)(kP1Stages - 1) * kThreads, st == 0 ? kP1Stages - 1 : st - 1);
+    cp_async_wait<kP1Stages - 1>();  // quad j has landed
+    if (j < n) {
+      const size_t o = (size_t)st * kP1StageBytes;
+      float g[4];
+      if constexpr (GD == LUMA_F32) {
+        const float4 v = *reinterpret_cast<const float4*>(sg + o);
+        g[0] = v.x; g[1] = v.y; g[2] = v.z; g[3] = v.w;
+      } else {
+        const uint2 v = *reinterpret_cast<const uint2*>(sg + o);
+        const uint32_t h[4] = {v.x & 0xFFFFu, v.x >> 16, v.y & 0xFFFFu, v.y >> 16};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          g[e] = (GD == LUMA_BF16) ? __uint_as_float(h[e] << 16)
+                                   : __half2float(__ushort_as_half((unsigned short)h[e]));
+      }
+      const uint2 qm = *reinterpret_cast<const uint2*>(sm + o);
+      const uint2 qw = *reinterpret_cast<const uint2*>(sw + o);
+      const uint32_t qmw[2] = {qm.x, qm.y}, qww[2] = {qw.x, qw.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t wm = qmw[e >> 1] >> (16 * (e & 1));
+        const uint32_t ww = (qww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+        pass1_elem(c, lut, g[e], (int)(int16_t)(uint16_t)wm, ww, ms);
+      }
+    }
+    st = st == kP1Stages - 1 ? 0 : st + 1;
+    ms.warp_sync_bounds();
+  }
+  cp_async_wait<0>();  // no copy left in flight into the stages
 }
 
 // Two consecutive elements (one Philox block) of a stream as floats.
@@ -1272,10 +1351,27 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
 
     if (!PASS2) {
       MaxSearch ms;
-      switch (d.grad_dtype) {
-        case LUMA_F32: pass1_octets<LUMA_F32>(d, c, lut, o_lo, o_hi, ms); break;
-        case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, lut, o_lo, o_hi, ms); break;
-        default: pass1_octets<LUMA_F16>(d, c, lut, o_lo, o_hi, ms); break;
+      // Staged loop for the complete octets of aligned tensors at step >= 2
+      // (the staging area exists whenever the kernel has its shared memory,
+      // i.e. lut_ok); plain loads for the rest.
+      int64_t ob = o_lo;
+      if (lut_ok && !c.init && d.vec_ok != 0) {
+        const int64_t o_full = min(o_hi, d.numel / 8);
+        if (o_full > o_lo) {
+          switch (d.grad_dtype) {
+            case LUMA_F32: pass1_staged<LUMA_F32>(d, c, lut, 2 * o_lo, 2 * o_full, ms); break;
+            case LUMA_BF16: pass1_staged<LUMA_BF16>(d, c, lut, 2 * o_lo, 2 * o_full, ms); break;
+            default: pass1_staged<LUMA_F16>(d, c, lut, 2 * o_lo, 2 * o_full, ms); break;
+          }
+          ob = o_full;
+        }
+      }
+      if (ob < o_hi) {
+        switch (d.grad_dtype) {
+          case LUMA_F32: pass1_octets<LUMA_F32>(d, c, lut, ob, o_hi, ms); break;
+          case LUMA_BF16: pass1_octets<LUMA_BF16>(d, c, lut, ob, o_hi, ms); break;
+          default: pass1_octets<LUMA_F16>(d, c, lut, ob, o_hi, ms); break;
+        }
       }
       uint32_t am = ms.am, av = ms.av;
       am = __reduce_max_sync(0xffffffffu, am);
@@ -1444,20 +1540,20 @@ int device_info(DeviceInfo** out) {
                   dev, prop.major, prop.minor);
     }
     e = cudaFuncSetAttribute(luma_pass_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kLutBytes);
+                             (int)kPass1SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass1)");
     e = cudaFuncSetAttribute(luma_pass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kPass2SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2)");
     e = cudaFuncSetAttribute(luma_pass_kernel<false, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLutBytes);
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPass1SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass1 noalloc)");
     e = cudaFuncSetAttribute(luma_pass_kernel<true, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPass2SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pass2 noalloc)");
     int b1 = 0, b2 = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b1, luma_pass_kernel<false>, kThreadsPass1,
-                                                      kLutBytes);
+                                                      kPass1SmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "occupancy(pass1)");
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b2, luma_pass_kernel<true>, kThreadsPass2,
                                                       kPass2SmemBytes);
@@ -1549,7 +1645,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
   luma_pass_kernel<false><<<grid_for(a.total_octets, kThreadsPass1, cap(di->ctas_pass1, a.max_ctas)), kThreadsPass1,
-                            kLutBytes, s>>>(a, 1, nullptr);
+                            kPass1SmemBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 1");
   if (a.events[1]) {
@@ -1686,7 +1782,7 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
   }
   luma_pass_kernel<false, true><<<grid_for(a.total_octets, kThreadsPass1, cap(di->ctas_pass1, a.max_ctas)),
-                                  kThreadsPass1, kLutBytes, s>>>(a, 1, acc);
+                                  kThreadsPass1, kPass1SmemBytes, s>>>(a, 1, acc);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 1 (noalloc)");
   if (a.events[1]) {
