@@ -1073,13 +1073,15 @@ __device__ __forceinline__ bool hot_segment(const SegShared& s) {
 }
 
 // pass2_elem for the steady state; sets `rare` when the element's results may
-// differ from pass2_elem's (they are then discarded).
+// differ from pass2_elem's (they are then discarded).  Every value of an
+// element that is not marked is finite, so the NaN-keeping clamps of the
+// general code become plain fminf / fmaxf here.
 __device__ __forceinline__ void pass2_elem_hot(const Consts& c, const float* lut, float g, float& p,
                                                uint32_t& qm, uint32_t& qw, float um, float uw,
                                                bool& rare) {
   const float m = decode_m_lut((int)(int16_t)(uint16_t)qm, lut);
   float t = __fsub_rn(rcp_cr(__fmul_rn(c.o_wmin, expf(__fmul_rn((float)qw, c.o_dw)))), c.eps32);
-  t = t < 0.0f ? 0.0f : t;
+  t = fmaxf(t, 0.0f);
   const float v = __fmul_rn(t, t);
   const float mn = __fadd_rn(__fmul_rn(c.beta1, m), __fmul_rn(c.omb1, g));
   const float vn = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, __fmul_rn(g, g)));
@@ -1094,30 +1096,27 @@ __device__ __forceinline__ void pass2_elem_hot(const Consts& c, const float* lut
   }
   {  // quant_m
     const float a = fabsf(mn);
-    const float ac = a > c.n_sm32 ? c.n_sm32 : a;
+    const float ac = fminf(a, c.n_sm32);
     const float y = __fmul_rn(log1pf(ac), c.n_inv_dm);
     const float fy = floorf(y);
     const float x = __fmul_rn(__fsub_rn(y, fy), c.n_dm);
     const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
     const float diff = __fsub_rn(um, __fmul_rn(e, c.inv_zm24));
     rare |= !(fabsf(diff) > c.margin_m);
-    float r = __fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f);
-    r = r > (float)LUMA_K_M ? (float)LUMA_K_M : r;
+    const float r = fminf(__fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f), (float)LUMA_K_M);
     const int ri = (int)r;
     qm = (uint32_t)(uint16_t)(int16_t)(mn < 0.0f ? -ri : ri);
   }
   {  // quant_w
     const float sq = v_ok ? sqrt_cr(vn) : 0.0f;
-    float w = rcp_cr(__fadd_rn(sq, c.eps32));
-    w = w < c.n_wmin ? c.n_wmin : (w > c.w_max ? c.w_max : w);
+    const float w = fminf(fmaxf(rcp_cr(__fadd_rn(sq, c.eps32)), c.n_wmin), c.w_max);
     const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
     const float fy = floorf(y);
     const float x = __fmul_rn(__fsub_rn(y, fy), c.n_dw);
     const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
     const float diff = __fsub_rn(uw, __fmul_rn(e, c.inv_zw24));
     rare |= !(fabsf(diff) > c.margin_w);
-    float r = __fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f);
-    r = r < 0.0f ? 0.0f : (r > (float)LUMA_K_W ? (float)LUMA_K_W : r);
+    const float r = fminf(fmaxf(__fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f), 0.0f), (float)LUMA_K_W);
     qw = (uint32_t)(int)r;
   }
 }
