@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LUMA_ABI_VERSION 2
+#define LUMA_ABI_VERSION 3
 
 /* Quantization grid constants (reference config.py:23-25). */
 #define LUMA_K_M 32767        /* signed int16 magnitude of Q_m        */
@@ -168,6 +168,19 @@ typedef struct LumaStepArgs {
                                          work on other streams (e.g. an NCCL
                                          all-gather of a previous bucket)   */
   int32_t               reserved;
+  int64_t*              step_counters; /* NULL: each descriptor's step is its
+                                         row's `step`.  Non-NULL (capturable
+                                         mode, for CUDA-graph replay): device
+                                         step counts indexed by slot; a
+                                         descriptor runs step t =
+                                         step_counters[desc.slot] + 1 with row
+                                         rows[desc.row + t - 1], and the call
+                                         ends with that count = t.  A row
+                                         index past n_rows skips the
+                                         descriptor and raises
+                                         LUMA_KERR_ROW_RANGE.  The reference
+                                         keeps the same count in a device
+                                         tensor (optimizer.py:382-387)       */
 } LumaStepArgs;
 
 /*
@@ -277,6 +290,15 @@ int luma_struct_sizes(int64_t* out, int n);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* luma_last_error(void);
+
+/*
+ * Kernel error flags of the current device (bits below), raised by the step
+ * kernels for conditions only the device sees: in capturable mode, a step
+ * count whose row lies past the row table (the descriptor was skipped).
+ * Synchronises the device; with `clear` != 0 the flags are reset afterwards.
+ */
+#define LUMA_KERR_ROW_RANGE 1u
+int luma_error_flags(uint32_t* out, int clear);
 
 #ifdef __cplusplus
 }

@@ -16,7 +16,7 @@ import numpy as np
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libluma_b200.so")
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 LUMA_OK = 0
 LUMA_ERR_INVALID = 1
@@ -73,6 +73,7 @@ class LumaStepArgs(ctypes.Structure):
         ("events", ctypes.c_void_p * 3),
         ("max_ctas", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
+        ("step_counters", ctypes.c_void_p),
     ]
 
 
@@ -81,7 +82,10 @@ EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
 
 EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_quantize",
             "luma_abi_version", "luma_struct_sizes", "luma_last_error", "luma_arith_selfcheck",
-            "luma_ipc_export", "luma_ipc_open", "luma_ipc_close", "luma_copy_async")
+            "luma_ipc_export", "luma_ipc_open", "luma_ipc_close", "luma_copy_async",
+            "luma_error_flags")
+
+KERR_ROW_RANGE = 1  # LUMA_KERR_ROW_RANGE
 
 NOALLOC_MAX_DESCS = 4096  # LUMA_NOALLOC_MAX_DESCS
 
@@ -125,6 +129,8 @@ def lib() -> ctypes.CDLL:
         h.luma_copy_async.restype = ctypes.c_int
         h.luma_copy_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                       ctypes.c_void_p]
+        h.luma_error_flags.restype = ctypes.c_int
+        h.luma_error_flags.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
         h.luma_step.restype = ctypes.c_int
         h.luma_step.argtypes = [ctypes.POINTER(LumaStepArgs), ctypes.c_void_p]
         h.luma_step_noalloc.restype = ctypes.c_int
@@ -184,6 +190,13 @@ def copy_async(dst: int, src: int, nbytes: int, stream) -> None:
     """One cudaMemcpyAsync (copy engine) of nbytes from src to dst on `stream`."""
     check(lib().luma_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes,
                                 ctypes.c_void_p(stream.cuda_stream)), "luma_copy_async")
+
+
+def kernel_error_flags(clear: bool = False) -> int:
+    """LUMA_KERR_* flags the step kernels raised on the current device (synchronises)."""
+    out = ctypes.c_uint32(0)
+    check(lib().luma_error_flags(ctypes.byref(out), int(clear)), "luma_error_flags")
+    return out.value
 
 
 def check(status: int, what: str) -> None:

@@ -47,6 +47,7 @@ static_assert(sizeof(LumaTensorDesc) == 96, "LumaTensorDesc layout");
 static_assert(sizeof(LumaStepRow) == 56, "LumaStepRow layout");
 static_assert(sizeof(LumaGrid) == 64, "LumaGrid layout");
 static_assert(sizeof(LumaSlot) == 144, "LumaSlot layout");
+static_assert(sizeof(LumaStepArgs) == 88, "LumaStepArgs layout");
 
 namespace {
 
@@ -98,6 +99,9 @@ static_assert(sizeof(PassAccum) == 16, "PassAccum layout");
 // Host code must not use this name as a device address; the set-up in
 // noalloc_scratch() fetches the address with cudaGetSymbolAddress.
 static __device__ __align__(256) PassAccum g_noalloc_accum[LUMA_NOALLOC_MAX_DESCS];
+
+// LUMA_KERR_* flags raised by the kernels (read by luma_error_flags).
+static __device__ unsigned int g_kernel_error = 0u;
 
 // ---------------------------------------------------------------------------
 // Error reporting
@@ -542,6 +546,7 @@ struct SegShared {
   LumaGrid dec;
   LumaGrid enc;
   int64_t next_pos;
+  int skip;  // capturable mode: the step's row is outside the table
 };
 
 // The CTA's segment state and decode table.  At namespace scope so that the
@@ -1297,7 +1302,21 @@ __device__ int find_desc(const LumaTensorDesc* descs, int n, int64_t pos) {
 // Thread 0: load descriptor `di`, its row and grids into shared memory.
 __device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShared& s) {
   s.d = a.descs[di];
-  s.row = a.rows[s.d.row];
+  s.skip = 0;
+  if (a.step_counters != nullptr) {
+    // Capturable mode: the step count lives on the device; the row of step t
+    // is entry t - 1 of the descriptor's block of the row table.
+    const int64_t t = a.step_counters[s.d.slot] + 1;
+    const int64_t r = (int64_t)s.d.row + t - 1;
+    if (t < 1 || r >= (int64_t)a.n_rows) {
+      s.skip = 1;
+      atomicOr(&g_kernel_error, (unsigned int)LUMA_KERR_ROW_RANGE);
+      return;
+    }
+    s.row = a.rows[r];
+  } else {
+    s.row = a.rows[s.d.row];
+  }
   const LumaSlot* slot = a.slots + s.d.slot;
   const int64_t t = s.row.step;
   if (t != 1) {
@@ -1337,6 +1356,12 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
     const int64_t n_oct = (d.numel + 7) / 8;
     const int64_t o_lo = pos - d.oct_begin;
     const int64_t o_hi = min(hi - d.oct_begin, n_oct);
+    if (s.skip) {  // (uniform) no row for this step: leave the tensor as it is
+      __syncthreads();
+      pos = d.oct_begin + o_hi;
+      ++di;
+      continue;
+    }
     Consts c;
     fill_consts(s, PASS2, c);
     // Decode table for long segments of quantized (t >= 2) tensors.
@@ -1425,6 +1450,14 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
     pos = d.oct_begin + o_hi;
     ++di;
   }
+}
+
+// Capturable mode: the step count of every descriptor's slot advances by one
+// after pass 2 (each slot appears in at most one descriptor of a call).
+__global__ void __launch_bounds__(kThreads) luma_count_steps_kernel(const LumaTensorDesc* descs,
+                                                                   int n, int64_t* counters) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i < n) counters[descs[i].slot] += 1;
 }
 
 __global__ void __launch_bounds__(kThreads) luma_decode_kernel(
@@ -1613,6 +1646,21 @@ int luma_abi_version(void) { return LUMA_ABI_VERSION; }
 
 const char* luma_last_error(void) { return luma_g_err; }
 
+int luma_error_flags(uint32_t* out, int clear) {
+  luma_g_err[0] = '\0';
+  if (out == nullptr) return fail(LUMA_ERR_INVALID, "luma_error_flags: out is null");
+  unsigned int v = 0u;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_kernel_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(error flags)");
+  if (clear && v != 0u) {
+    const unsigned int zero = 0u;
+    e = cudaMemcpyToSymbol(g_kernel_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(error flags)");
+  }
+  *out = v;
+  return LUMA_OK;
+}
+
 int luma_struct_sizes(int64_t* out, int n) {
   const int64_t sizes[5] = {(int64_t)sizeof(LumaTensorDesc), (int64_t)sizeof(LumaStepRow),
                             (int64_t)sizeof(LumaGrid), (int64_t)sizeof(LumaSlot),
@@ -1655,6 +1703,12 @@ int luma_step(const LumaStepArgs* args, void* stream) {
                            kPass2SmemBytes, s>>>(a, 1, nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
+  if (a.step_counters != nullptr) {
+    luma_count_steps_kernel<<<(a.n_desc + kThreads - 1) / kThreads, kThreads, 0, s>>>(
+        a.descs, a.n_desc, a.step_counters);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch step count");
+  }
   if (a.events[2]) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[2]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
@@ -1792,6 +1846,12 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
                                  kThreadsPass2, kPass2SmemBytes, s>>>(a, 1, acc);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2 (noalloc)");
+  if (a.step_counters != nullptr) {
+    luma_count_steps_kernel<<<(a.n_desc + kThreads - 1) / kThreads, kThreads, 0, s>>>(
+        a.descs, a.n_desc, a.step_counters);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch step count");
+  }
   if (a.events[2]) {
     e = cudaEventRecord(static_cast<cudaEvent_t>(a.events[2]), s);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");

@@ -12,6 +12,12 @@ allocated through torch's caching allocator, never inside the step kernels):
 * ``rows``   — the LumaStepRow table of this step, uploaded every step from
   a small ring of pinned host buffers (an event guards each ring entry, so a
   buffer is rewritten only after its copy has executed).
+
+Capturable mode (CUDA-graph replay) replaces the per-step rows by a fixed
+device table the caller builds once (one block of rows per param group, one
+row per step) and adds ``counters``: one int64 step count per slot on the
+device, advanced by the library after each step, so a replayed launch finds
+its step, row and seed without host work.
 """
 
 from __future__ import annotations
@@ -88,6 +94,7 @@ class DeviceEngine:
         self.device = device
         self.n_slots = 0
         self.slots = torch.zeros(0, dtype=torch.uint8, device=device)
+        self.counters = torch.zeros(0, dtype=torch.int64, device=device)
         self.rows_dev = torch.zeros(ROW_DTYPE.itemsize * 4, dtype=torch.uint8, device=device)
         self._ring = []
         self._ring_i = 0
@@ -103,9 +110,12 @@ class DeviceEngine:
             return
         cap = max(n, 2 * self.n_slots, 16)
         new = torch.zeros(cap * SLOT_DTYPE.itemsize, dtype=torch.uint8, device=self.device)
+        cnt = torch.zeros(cap, dtype=torch.int64, device=self.device)
         if self.n_slots:
             new[: self.slots.numel()].copy_(self.slots)
+            cnt[: self.counters.numel()].copy_(self.counters)
         self.slots = new
+        self.counters = cnt
         self.n_slots = cap
         self._sig = None  # slot base pointer changed
 
@@ -143,26 +153,39 @@ class DeviceEngine:
             self.rows_dev[:nbytes].copy_(buf[:nbytes], non_blocking=True)
             ev.record(stream)
 
-    def step(self, segs: list[Segment], rows: np.ndarray, base_seed: int,
-             stream: torch.cuda.Stream | None = None, events=None, max_ctas: int = 0) -> None:
+    def step(self, segs: list[Segment], rows: np.ndarray | None, base_seed: int,
+             stream: torch.cuda.Stream | None = None, events=None, max_ctas: int = 0,
+             row_table: torch.Tensor | None = None) -> None:
+        """Launch one step.  `rows`: this step's LumaStepRow records (uploaded);
+        or, in capturable mode, `row_table`: a fixed device table (rows=None),
+        with the step counts taken from and advanced in ``self.counters``."""
         if not segs:
             return
         if stream is None:
             stream = torch.cuda.current_stream(self.device)
         sig = tuple(s.key() for s in segs)
         if sig != self._sig:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("LUMA: the set of parameters with gradients changed while a "
+                                   "CUDA graph was being captured")
             table, total = build_desc_table(segs)
             self._descs_dev = torch.from_numpy(table.view(np.uint8).copy()).to(self.device)
             self._n_desc = len(segs)
             self._total_oct = total
             self._sig = sig
-        self._upload_rows(rows, stream)
         a = self._args
+        if row_table is None:
+            self._upload_rows(rows, stream)
+            a.rows = self.rows_dev.data_ptr()
+            a.n_rows = len(rows)
+            a.step_counters = None
+        else:
+            a.rows = row_table.data_ptr()
+            a.n_rows = row_table.numel() // ROW_DTYPE.itemsize
+            a.step_counters = self.counters.data_ptr()
         a.descs = self._descs_dev.data_ptr()
         a.slots = self.slots.data_ptr()
-        a.rows = self.rows_dev.data_ptr()
         a.n_desc = self._n_desc
-        a.n_rows = len(rows)
         a.total_octets = self._total_oct
         a.base_seed = ctypes.c_int64(int(base_seed)).value
         for i in range(3):

@@ -84,5 +84,30 @@ def step_row(step: int, lr: float, beta1: float, beta2: float, eps: float,
                 _f32(1.0 / eps), _f32(0.0))
 
 
+def step_rows(steps: np.ndarray, lr: float, beta1: float, beta2: float, eps: float,
+              weight_decay: float) -> np.ndarray:
+    """``step_row`` for many steps at once (numpy float64 ``power`` calls the
+    same libm ``pow`` as Python's ``**``; the other operations are IEEE)."""
+    t = np.asarray(steps, dtype=np.int64)
+    tf = t.astype(np.float64)
+    bc1 = 1.0 - np.power(beta1, tf)
+    bc2 = 1.0 - np.power(beta2, tf)
+    out = np.zeros(t.shape, dtype=ROW_DTYPE)
+    with np.errstate(over="ignore", divide="ignore", invalid="ignore"):
+        eta = lr / bc1
+        out["step"] = t
+        out["eps"] = eps
+        out["beta1"] = _f32(beta1)
+        out["omb1"] = _f32(1.0 - beta1)
+        out["beta2"] = _f32(beta2)
+        out["omb2"] = _f32(1.0 - beta2)
+        out["decay"] = _f32(1.0 - weight_decay * lr)
+        out["neg_eta"] = (-eta).astype(np.float32)
+        out["inv_bc2"] = (1.0 / bc2).astype(np.float32)
+        out["eps32"] = _f32(eps)
+        out["w_max"] = _f32(1.0 / eps)
+    return out
+
+
 def rows_array(rows: list[tuple]) -> np.ndarray:
     return np.array(rows, dtype=ROW_DTYPE)

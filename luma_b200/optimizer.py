@@ -25,7 +25,7 @@ from torch.optim import Optimizer
 
 from . import _lib
 from .engine import DeviceEngine, Segment
-from .hostmath import SCALE_FLOOR_M, grid_record, precompute, rows_array, step_row
+from .hostmath import SCALE_FLOOR_M, grid_record, precompute, rows_array, step_row, step_rows
 
 _BACKENDS = {"auto", "cuda", "triton"}
 _PARAM_DTYPES = (torch.float32, torch.bfloat16)
@@ -43,6 +43,17 @@ class LUMA(Optimizer):
     eps : float, denominator term (default 1e-8).
     weight_decay : float, decoupled weight decay (default 0.01).
     backend : "auto" | "cuda" | "triton" — all run the CUDA kernels.
+    capturable : bool (default False).  True makes ``step()`` safe to capture
+        in a CUDA graph and replay (like the reference's Triton backend,
+        optimizer.py:18-19, 382-387): the step count of every parameter lives
+        on the device and advances inside the launch, and the per-step scalars
+        come from a device table with one row per (param group, step) for
+        steps 1..capture_steps, built from the group hyper-parameters.  After
+        changing a hyper-parameter (an LR schedule), call
+        ``refresh_capturable_rows()`` outside the graph; replays read the
+        refreshed table.  Take at least one eager step before capturing.
+    capture_steps : int (default 2**17), rows per group in capturable mode; a
+        step past it is skipped and reported by ``kernel_error_flags()``.
 
     Params may be float32 or bfloat16 (bf16 params are updated in float32
     arithmetic and rounded once to bf16, nearest even); grads float32,
@@ -55,7 +66,8 @@ class LUMA(Optimizer):
     """
 
     def __init__(self, params, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
-                 eps: float = 1e-8, weight_decay: float = 0.01, backend: str = "auto"):
+                 eps: float = 1e-8, weight_decay: float = 0.01, backend: str = "auto",
+                 capturable: bool = False, capture_steps: int = 1 << 17):
         # Validation order and messages follow optimizer.py:80-89.
         if lr < 0.0:
             raise ValueError(f"Invalid learning rate: {lr}")
@@ -82,6 +94,11 @@ class LUMA(Optimizer):
         self._slot_count: dict[torch.device, int] = {}
         self._draw_hook = None
         self._step_events = None  # optional (ev0, ev1, ev2) cudaEvent_t handles, timing hook
+        if capture_steps < 1:
+            raise ValueError(f"Invalid capture_steps: {capture_steps}")
+        self.capturable = bool(capturable)
+        self.capture_steps = int(capture_steps)
+        self._row_tables: dict[torch.device, tuple[tuple, torch.Tensor]] = {}
 
     # ------------------------------------------------------------------
     # helpers
@@ -117,8 +134,90 @@ class LUMA(Optimizer):
         injected-draw path).  ``None`` restores Philox."""
         self._draw_hook = fn
 
+    # -- capturable mode -----------------------------------------------------
+    def _hyper_key(self) -> tuple:
+        return tuple((g["lr"], g["betas"][0], g["betas"][1], g["eps"], g["weight_decay"])
+                     for g in self.param_groups)
+
+    def _row_table(self, device: torch.device) -> torch.Tensor:
+        """Device LumaStepRow table, capture_steps rows per group (built on
+        first use and whenever a hyper-parameter changed)."""
+        key = self._hyper_key()
+        cached = self._row_tables.get(device)
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("LUMA(capturable=True): hyper-parameters changed (or no eager "
+                               "step was taken) before CUDA graph capture; call "
+                               "refresh_capturable_rows() outside the graph")
+        steps = np.arange(1, self.capture_steps + 1, dtype=np.int64)
+        table = np.concatenate([step_rows(steps, *k) for k in key])
+        host = torch.from_numpy(table.view(np.uint8).copy())
+        if cached is not None and cached[1].numel() == host.numel():
+            dev_tab = cached[1]  # same size: refresh in place (graphs hold this address)
+            dev_tab.copy_(host.to(device))
+        else:
+            dev_tab = host.to(device)
+        self._row_tables[device] = (key, dev_tab)
+        return dev_tab
+
+    @torch.no_grad()
+    def refresh_capturable_rows(self) -> None:
+        """Rebuild the capturable-mode row tables from the current group
+        hyper-parameters (in place, so captured graphs see the new values)."""
+        for dev in list(self._row_tables):
+            self._row_table(dev)
+
+    def _sync_steps(self) -> None:
+        """Capturable mode: state["step"] from the device step counters."""
+        if not self.capturable:
+            return
+        counts = {dev: eng.counters.cpu() for dev, eng in self._engines.items()}
+        for group in self.param_groups:
+            for p in group["params"]:
+                st = self.state.get(p)
+                if not st or "_slot" not in st:
+                    continue
+                st["step"] = int(counts[self._unwrap_tensor(p).device][st["_slot"]])
+
+    def _set_step_count(self, device: torch.device, slot: int, step: int) -> None:
+        if self.capturable:
+            self._engine(device).counters[slot] = step
+
+    def step_op_args(self) -> dict:
+        """Capturable mode: keyword arguments of ``torch.ops.luma_b200.step``
+        that step this optimizer's parameters exactly as ``step()`` does (the
+        parameters with gradients and their state as of the last eager
+        ``step()``; one device)."""
+        if not self.capturable:
+            raise RuntimeError("step_op_args() needs LUMA(..., capturable=True)")
+        if len(self._engines) != 1:
+            raise RuntimeError("step_op_args() needs exactly one device with stepped params")
+        (dev, eng), = self._engines.items()
+        out = dict(params=[], grads=[], q_m=[], q_w=[], param_ids=[], slot_ids=[], row_bases=[])
+        for gi, group in enumerate(self.param_groups):
+            for p in group["params"]:
+                st = self.state.get(p)
+                if p.grad is None or not st or "_slot" not in st:
+                    continue
+                out["params"].append(self._unwrap_tensor(p))
+                out["grads"].append(self._unwrap_tensor(p.grad))
+                out["q_m"].append(st["Q_m"])
+                out["q_w"].append(st["Q_w"])
+                out["param_ids"].append(st["param_id"])
+                out["slot_ids"].append(st["_slot"])
+                out["row_bases"].append(gi * self.capture_steps)
+        out.update(slots=eng.slots, counters=eng.counters, row_table=self._row_table(dev),
+                   base_seed=self._base_seed)
+        return out
+
+    def kernel_error_flags(self, clear: bool = False) -> int:
+        """LUMA_KERR_* flags raised by the step kernels on the current device."""
+        return _lib.kernel_error_flags(clear)
+
     def _grid_scales(self) -> dict[int, tuple[float, float]]:
         """(S_m, S_v) per state-holding param, read from the device slots."""
+        self._sync_steps()
         out = {}
         host = {dev: eng.read_slots() for dev, eng in self._engines.items()}
         for group in self.param_groups:
@@ -197,6 +296,7 @@ class LUMA(Optimizer):
             eng = self._engine(param.device)
             eng.reset_slot(slot)
             eng.write_grid(slot, st["step"] & 1, grid_record(st["S_m"], st["S_v"], eps_of[id(p)]))
+            self._set_step_count(param.device, slot, st["step"])
             st.pop("S_m")
             st.pop("S_v")
 
@@ -306,6 +406,7 @@ class LUMA(Optimizer):
             eng = self._engine(device)
             eng.reset_slot(slot)
             eng.write_grid(slot, step & 1, grid[0])
+            self._set_step_count(device, slot, step)
             state.pop("S_m", None)
             state.pop("S_v", None)
             if um is not None:
@@ -314,9 +415,14 @@ class LUMA(Optimizer):
     # ------------------------------------------------------------------
     # step (optimizer.py:413-524)
     # ------------------------------------------------------------------
+    @torch.compiler.disable
     @torch.no_grad()
     def step(self, closure=None):
-        """One optimisation step for every parameter with a gradient."""
+        """One optimisation step for every parameter with a gradient.
+
+        Under ``torch.compile`` this method runs eagerly (one graph break at
+        the call): its host side is table bookkeeping for a single library
+        call.  ``torch.ops.luma_b200.step`` is the traceable form."""
         loss = None
         if closure is not None:
             with torch.enable_grad():
@@ -370,16 +476,25 @@ class LUMA(Optimizer):
             if "_slot" not in state:
                 state["_slot"] = self._new_slot(param.device)
             segs, rowmap = per_dev.setdefault(param.device, ([], {}))
-            row = rowmap.setdefault((gi, t), len(rowmap))
+            if self.capturable:
+                row = gi * self.capture_steps  # the group's block of the row table
+            else:
+                row = rowmap.setdefault((gi, t), len(rowmap))
             seg = Segment(param.view(-1), grad.view(-1), state["Q_m"].view(-1),
                           state["Q_w"].view(-1), state["param_id"], row, state["_slot"])
             if self._draw_hook is not None:
+                if self.capturable:
+                    raise RuntimeError("the draw hook is not available in capturable mode")
                 um, uw = self._draw_hook(state["param_id"], t, param)
                 seg.u_m = um.reshape(-1)
                 seg.u_w = uw.reshape(-1)
             segs.append(seg)
 
         for dev, (segs, rowmap) in per_dev.items():
+            if self.capturable:
+                self._engine(dev).step(segs, None, self._base_seed, events=self._step_events,
+                                       row_table=self._row_table(dev))
+                continue
             rows = [None] * len(rowmap)
             for (gi, t), r in rowmap.items():
                 g = self.param_groups[gi]
