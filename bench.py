@@ -305,8 +305,10 @@ def run_luma(args, rank, world, local_rank):
         total_ms = float(t.item())
     ms_per_step = total_ms / K
 
-    # e2e: grads from pinned host memory each step, step through the public
-    # API, read the new per-tensor scales back.
+    # e2e: every step's grads copied from pinned host memory, the step through
+    # the public API (LUMA.step), the new per-tensor scales read back to pinned
+    # host memory.  Two grad buffers: the upload of step k+1's grads (copy
+    # engine, side stream) overlaps step k's kernels.
     e2e = None
     if not args.no_e2e:
         try:
@@ -316,18 +318,44 @@ def run_luma(args, rank, world, local_rank):
             h2d = sum(h.numel() * h.element_size() for h in host)
             eng = next(iter(opt._engines.values()))
             d2h = eng.slots.numel()
+            bufs = [grads, [torch.empty_like(g) for g in grads]]
+            out = [torch.empty(d2h, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+            up = torch.cuda.Stream()
+            main = torch.cuda.current_stream()
+            copied = [torch.cuda.Event(), torch.cuda.Event()]
+            stepped = [torch.cuda.Event(), torch.cuda.Event()]
             E = max(2, min(K, 5))
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            for _ in range(E):
-                for h, g in zip(host, grads):
-                    g.copy_(h, non_blocking=True)
+
+            def upload(k):
+                b = k % 2
+                with torch.cuda.stream(up):
+                    if k >= 2:
+                        up.wait_event(stepped[b])  # step k-2 is done with this buffer
+                    for h, g in zip(host, bufs[b]):
+                        g.copy_(h, non_blocking=True)
+                    copied[b].record(up)
+
+            upload(0)
+            for k in range(E):
+                if k + 1 < E:
+                    upload(k + 1)
+                b = k % 2
+                main.wait_event(copied[b])
+                for p, g in zip(params, bufs[b]):
+                    p.grad = g
                 opt.step()
-                eng.read_slots()  # D2H of S_m/S_v of every tensor (synchronises)
+                out[b].copy_(eng.slots, non_blocking=True)  # this step's S_m / S_v to host
+                stepped[b].record(main)
+            torch.cuda.synchronize()
             el = time.perf_counter() - t0
             e2e = {"value": round(n_params * E / el / 1e9, 3), "unit": "Gparams/s",
-                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": E}
-            del host
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": E,
+                   "pipelining": "double-buffered grads: step k+1's upload overlaps step k"}
+            for p, g in zip(params, grads):
+                p.grad = g
+            del host, bufs, out
         except Exception as exc:  # noqa: BLE001
             e2e = {"value": None, "unit": "Gparams/s", "error": str(exc)[:200]}
 
@@ -402,22 +430,48 @@ def run_zero(args, rank, world, local_rank):
     ms_gather, _ = timed(opt.gather)
     e2e = None
     if not args.no_e2e:
+        # as at N=1: double-buffered grad uploads, scales read back every step
         host = torch.empty(gshard.shape, dtype=gshard.dtype, pin_memory=True)
         host.copy_(gshard)
+        bufs = [gshard, torch.empty_like(gshard)]
+        d2h = sum(e.slots.numel() for e in opt.engines)
+        out = [[torch.empty(e.slots.numel(), dtype=torch.uint8, pin_memory=True)
+                for e in opt.engines] for _ in range(2)]
+        up = torch.cuda.Stream()
+        main = torch.cuda.current_stream()
+        copied = [torch.cuda.Event(), torch.cuda.Event()]
+        stepped = [torch.cuda.Event(), torch.cuda.Event()]
         E = max(2, min(K, 5))
+
+        def upload(k):
+            b = k % 2
+            with torch.cuda.stream(up):
+                if k >= 2:
+                    up.wait_event(stepped[b])
+                bufs[b].copy_(host, non_blocking=True)
+                copied[b].record(up)
+
         dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        for _ in range(E):
-            gshard.copy_(host, non_blocking=True)
-            opt.step(gshard)
-            for eng in opt.engines:
-                eng.read_slots()
+        upload(0)
+        for k in range(E):
+            if k + 1 < E:
+                upload(k + 1)
+            b = k % 2
+            main.wait_event(copied[b])
+            opt.step(bufs[b])
+            for o, e in zip(out[b], opt.engines):
+                o.copy_(e.slots, non_blocking=True)
+            stepped[b].record(main)
+        torch.cuda.synchronize()
         el = torch.tensor([time.perf_counter() - t0], device=device)
         dist.all_reduce(el, op=dist.ReduceOp.MAX)
         e2e = {"value": round(n_params * E / float(el.item()) / 1e9, 3), "unit": "Gparams/s",
                "h2d_bytes_per_step": host.numel() * host.element_size(),
-               "d2h_bytes_per_step": sum(e.slots.numel() for e in opt.engines), "steps": E}
+               "d2h_bytes_per_step": d2h, "steps": E,
+               "pipelining": "double-buffered grad shards: step k+1's upload overlaps step k"}
+        del bufs, out, host
 
     opt.close()
     p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])

@@ -34,6 +34,7 @@ from ._lib import DESC_DTYPE, GRID_DTYPE, ROW_DTYPE, SLOT_DTYPE
 _DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
 _RING = 4
+_TABLE_CACHE = 4
 
 
 def dtype_code(dt: torch.dtype) -> int:
@@ -102,6 +103,7 @@ class DeviceEngine:
         self._descs_dev = None
         self._n_desc = 0
         self._total_oct = 0
+        self._tables: dict[tuple, tuple[torch.Tensor, int, int]] = {}  # sig -> (descs, n, octets)
         self._args = _lib.LumaStepArgs()
 
     # -- slots ---------------------------------------------------------------
@@ -118,6 +120,7 @@ class DeviceEngine:
         self.counters = cnt
         self.n_slots = cap
         self._sig = None  # slot base pointer changed
+        self._tables.clear()
 
     def write_grid(self, slot: int, parity: int, rec: np.ndarray) -> None:
         """Store one LumaGrid into grid[parity] of `slot` (stream-ordered)."""
@@ -165,13 +168,20 @@ class DeviceEngine:
             stream = torch.cuda.current_stream(self.device)
         sig = tuple(s.key() for s in segs)
         if sig != self._sig:
-            if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError("LUMA: the set of parameters with gradients changed while a "
-                                   "CUDA graph was being captured")
-            table, total = build_desc_table(segs)
-            self._descs_dev = torch.from_numpy(table.view(np.uint8).copy()).to(self.device)
-            self._n_desc = len(segs)
-            self._total_oct = total
+            # A few recent tables are kept, so callers that alternate grad
+            # buffers (double buffering) do not rebuild one every step.
+            hit = self._tables.get(sig)
+            if hit is None:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError("LUMA: the set of parameters with gradients changed while "
+                                       "a CUDA graph was being captured")
+                table, total = build_desc_table(segs)
+                hit = (torch.from_numpy(table.view(np.uint8).copy()).to(self.device), len(segs),
+                       total)
+                if len(self._tables) >= _TABLE_CACHE:
+                    self._tables.pop(next(iter(self._tables)))
+                self._tables[sig] = hit
+            self._descs_dev, self._n_desc, self._total_oct = hit
             self._sig = sig
         a = self._args
         if row_table is None:
