@@ -181,6 +181,15 @@ typedef struct LumaStepArgs {
                                          LUMA_KERR_ROW_RANGE.  The reference
                                          keeps the same count in a device
                                          tensor (optimizer.py:382-387)       */
+  const float*          grad_scale;   /* NULL, or a device float32 scalar c:
+                                         every grad element g is used as
+                                         round_to_grad_dtype(fl32(g) * c) —
+                                         exactly torch._foreach_mul_(grads, c)
+                                         as clip_grad_norm_ applies it
+                                         (reference usage: bench_nanogpt.py:
+                                         218, 225), fused into both passes
+                                         instead of a separate pass over the
+                                         grads; the grads are not modified  */
 } LumaStepArgs;
 
 /*

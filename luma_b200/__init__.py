@@ -8,6 +8,7 @@ two hand-written sm_100a kernels over all parameters (``libluma_b200.so``).
 from .config import K_M, K_W, SCALE_FLOOR_M, get_kernel_config
 from .optimizer import LUMA
 from . import torch_op  # registers torch.ops.luma_b200.step
+from .clip import clip_grad_coef
 
-__all__ = ["LUMA", "get_kernel_config", "K_M", "K_W", "SCALE_FLOOR_M"]
+__all__ = ["LUMA", "clip_grad_coef", "get_kernel_config", "K_M", "K_W", "SCALE_FLOOR_M"]
 __version__ = "0.1.0"

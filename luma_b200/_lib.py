@@ -74,6 +74,7 @@ class LumaStepArgs(ctypes.Structure):
         ("max_ctas", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
         ("step_counters", ctypes.c_void_p),
+        ("grad_scale", ctypes.c_void_p),
     ]
 
 

@@ -47,7 +47,7 @@ static_assert(sizeof(LumaTensorDesc) == 96, "LumaTensorDesc layout");
 static_assert(sizeof(LumaStepRow) == 56, "LumaStepRow layout");
 static_assert(sizeof(LumaGrid) == 64, "LumaGrid layout");
 static_assert(sizeof(LumaSlot) == 144, "LumaSlot layout");
-static_assert(sizeof(LumaStepArgs) == 88, "LumaStepArgs layout");
+static_assert(sizeof(LumaStepArgs) == 96, "LumaStepArgs layout");
 
 namespace {
 
@@ -215,6 +215,9 @@ __device__ __forceinline__ void cp_async_wait() {
 struct Consts {
   // step row
   float beta1, omb1, beta2, omb2, decay, neg_eta, inv_bc2, eps32, w_max;
+  // fused grad scaling (clip_grad_norm_'s coefficient), has_gscale != 0
+  float gscale;
+  int has_gscale;
   // decode grid (codes as stored)
   float o_dm, o_wmin, o_dw;
   // encode grid (this step's new scales), pass 2 only
@@ -261,6 +264,32 @@ __device__ __forceinline__ void ema(const Consts& c, float g, float m, float v,
   } else {
     mn = __fadd_rn(__fmul_rn(c.beta1, m), __fmul_rn(c.omb1, g));
     vn = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, g2));
+  }
+}
+
+// Fused grad scaling: g -> round_to_grad_dtype(fl32(g) * c), what
+// torch._foreach_mul_(grads, c) stores (clip_grad_norm_'s last step).
+template <int GD>
+__device__ __forceinline__ float scale_grad(float g, float c) {
+  const float x = __fmul_rn(g, c);
+  if (GD == LUMA_F32) return x;
+  if (GD == LUMA_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  return __half2float(__float2half_rn(x));
+}
+
+template <int GD, int N>
+__device__ __forceinline__ void scale_grads(const Consts& c, float (&g)[N]) {
+  if (c.has_gscale) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) g[j] = scale_grad<GD>(g[j], c.gscale);
+  }
+}
+
+template <int GD>
+__device__ __forceinline__ void scale_grads2(const Consts& c, float& g0, float& g1) {
+  if (c.has_gscale) {
+    g0 = scale_grad<GD>(g0, c.gscale);
+    g1 = scale_grad<GD>(g1, c.gscale);
   }
 }
 
@@ -547,6 +576,8 @@ struct SegShared {
   LumaGrid enc;
   int64_t next_pos;
   int skip;  // capturable mode: the step's row is outside the table
+  int has_gscale;  // grads are scaled by gscale (LumaStepArgs.grad_scale)
+  float gscale;
 };
 
 // The CTA's segment state and decode table.  At namespace scope so that the
@@ -559,6 +590,8 @@ __device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Cons
   c.decay = s.row.decay; c.neg_eta = s.row.neg_eta; c.inv_bc2 = s.row.inv_bc2;
   c.eps32 = s.row.eps32; c.w_max = s.row.w_max;
   c.init = (s.row.step == 1) ? 1 : 0;
+  c.gscale = s.gscale;
+  c.has_gscale = s.has_gscale;
   c.o_dm = s.dec.dm; c.o_wmin = s.dec.w_min; c.o_dw = s.dec.dw;
   if (pass2) {
     c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
@@ -649,6 +682,7 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
       const int n = rem < 8 ? (int)rem : 8;
       float g[8];
       load8<GD>(d.grad, e0, n, d.vec_ok != 0 && n == 8, g);
+      scale_grads<GD>(c, g);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (j < n) {
@@ -674,6 +708,7 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
       float g[8];
       uint16_t qm[8], qw[8];
       load8<GD>(d.grad, e0, n, vec, g);
+      scale_grads<GD>(c, g);
       load8_codes(d.q_m, e0, n, vec, qm);
       load8_codes(d.q_w, e0, n, vec, qw);
 #pragma unroll
@@ -733,6 +768,7 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
           g[e] = (GD == LUMA_BF16) ? __uint_as_float(h[e] << 16)
                                    : __half2float(__ushort_as_half((unsigned short)h[e]));
       }
+      scale_grads<GD>(c, g);
       const uint2 qm = *reinterpret_cast<const uint2*>(sm + o);
       const uint2 qw = *reinterpret_cast<const uint2*>(sw + o);
       const uint32_t qmw[2] = {qm.x, qm.y}, qww[2] = {qw.x, qw.y};
@@ -924,6 +960,7 @@ __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Const
     float p0, p1, g0, g1;
     unpack2<PD>(cur.p, p0, p1);
     unpack2<GD>(cur.g, g0, g1);
+    scale_grads2<GD>(c, g0, g1);
     uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
     uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
     float um0, um1, uw0, uw1;
@@ -967,6 +1004,7 @@ __device__ __forceinline__ void pass2_prefetch(const LumaTensorDesc& d, const Co
     float p0, p1, g0, g1;
     unpack2<PD>(cur.p, p0, p1);
     unpack2<GD>(cur.g, g0, g1);
+    scale_grads2<GD>(c, g0, g1);
     uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
     uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
     float um0, um1, uw0, uw1;
@@ -1022,6 +1060,7 @@ __device__ __forceinline__ void pass2_fast(const Consts& c, const float* lut, ui
     float p0, p1, g0, g1;
     unpack2<PD>(cur.p, p0, p1);
     unpack2<GD>(cur.g, g0, g1);
+    scale_grads2<GD>(c, g0, g1);
     uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
     uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
     const uint64_t ctr = ctr_base + (uint32_t)i;
@@ -1140,6 +1179,7 @@ __device__ __noinline__ void pass2_pair_exact(uint32_t k0, uint32_t k1, int64_t 
   float p0, p1, g0, g1;
   unpack2<PD>(r.p, p0, p1);
   unpack2<GD>(r.g, g0, g1);
+  scale_grads2<GD>(c, g0, g1);
   uint32_t qm0 = r.qm & 0xFFFFu, qm1 = r.qm >> 16;
   uint32_t qw0 = r.qw & 0xFFFFu, qw1 = r.qw >> 16;
   const uint64_t ctr = ((uint64_t)d.rng_offset >> 1) + (uint64_t)P;
@@ -1197,6 +1237,7 @@ __device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, c
     float p0, p1, g0, g1;
     unpack2<PD>(cur.p, p0, p1);
     unpack2<GD>(cur.g, g0, g1);
+    scale_grads2<GD>(c, g0, g1);
     uint32_t qm0 = cur.qm & 0xFFFFu, qm1 = cur.qm >> 16;
     uint32_t qw0 = cur.qw & 0xFFFFu, qw1 = cur.qw >> 16;
     const uint64_t ctr = ctr_base + (uint32_t)i;
@@ -1303,6 +1344,8 @@ __device__ int find_desc(const LumaTensorDesc* descs, int n, int64_t pos) {
 __device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShared& s) {
   s.d = a.descs[di];
   s.skip = 0;
+  s.has_gscale = a.grad_scale != nullptr;
+  s.gscale = a.grad_scale != nullptr ? *a.grad_scale : 1.0f;
   if (a.step_counters != nullptr) {
     // Capturable mode: the step count lives on the device; the row of step t
     // is entry t - 1 of the descriptor's block of the row table.

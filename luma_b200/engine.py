@@ -158,10 +158,13 @@ class DeviceEngine:
 
     def step(self, segs: list[Segment], rows: np.ndarray | None, base_seed: int,
              stream: torch.cuda.Stream | None = None, events=None, max_ctas: int = 0,
-             row_table: torch.Tensor | None = None) -> None:
+             row_table: torch.Tensor | None = None,
+             grad_scale: torch.Tensor | None = None) -> None:
         """Launch one step.  `rows`: this step's LumaStepRow records (uploaded);
         or, in capturable mode, `row_table`: a fixed device table (rows=None),
-        with the step counts taken from and advanced in ``self.counters``."""
+        with the step counts taken from and advanced in ``self.counters``.
+        `grad_scale`: optional float32 device scalar every grad is multiplied
+        by (in the grad's dtype) inside the kernels."""
         if not segs:
             return
         if stream is None:
@@ -201,5 +204,6 @@ class DeviceEngine:
         for i in range(3):
             a.events[i] = None if events is None else events[i]
         a.max_ctas = max_ctas
+        a.grad_scale = None if grad_scale is None else grad_scale.data_ptr()
         _lib.check(_lib.lib().luma_step(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)),
                    "luma_step")

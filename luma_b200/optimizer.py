@@ -99,6 +99,7 @@ class LUMA(Optimizer):
         self.capturable = bool(capturable)
         self.capture_steps = int(capture_steps)
         self._row_tables: dict[torch.device, tuple[tuple, torch.Tensor]] = {}
+        self._scale_refs: dict[torch.device, torch.Tensor] = {}
 
     # ------------------------------------------------------------------
     # helpers
@@ -417,12 +418,26 @@ class LUMA(Optimizer):
     # ------------------------------------------------------------------
     @torch.compiler.disable
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, *, grad_scale: torch.Tensor | None = None):
         """One optimisation step for every parameter with a gradient.
+
+        ``grad_scale``: optional one-element float32 / bfloat16 / float16
+        tensor c (the clip coefficient carries the grads' dtype); every grad
+        element g is then used as ``round_to_grad_dtype(fl32(g) * fl32(c))`` —
+        what ``torch._foreach_mul_(grads, c)`` would have stored — without
+        touching the grads.  With ``c`` from ``luma_b200.clip_grad_coef`` this fuses
+        ``clip_grad_norm_``'s rescaling pass into the step (bit-identical to
+        clipping first; the reference's training loop clips before every step,
+        benchmarks/bench_nanogpt.py:218-225).
 
         Under ``torch.compile`` this method runs eagerly (one graph break at
         the call): its host side is table bookkeeping for a single library
         call.  ``torch.ops.luma_b200.step`` is the traceable form."""
+        if grad_scale is not None:
+            if not isinstance(grad_scale, torch.Tensor) or grad_scale.numel() != 1 \
+                    or grad_scale.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+                raise ValueError("grad_scale must be a one-element float32, bfloat16 or "
+                                 "float16 tensor")
         loss = None
         if closure is not None:
             with torch.enable_grad():
@@ -491,9 +506,13 @@ class LUMA(Optimizer):
             segs.append(seg)
 
         for dev, (segs, rowmap) in per_dev.items():
+            gs = None
+            if grad_scale is not None:
+                gs = grad_scale.reshape(1).to(device=dev, dtype=torch.float32, non_blocking=True)
+                gs = self._keep_scale(dev, gs)
             if self.capturable:
                 self._engine(dev).step(segs, None, self._base_seed, events=self._step_events,
-                                       row_table=self._row_table(dev))
+                                       row_table=self._row_table(dev), grad_scale=gs)
                 continue
             rows = [None] * len(rowmap)
             for (gi, t), r in rowmap.items():
@@ -501,5 +520,11 @@ class LUMA(Optimizer):
                 rows[r] = step_row(t, g["lr"], g["betas"][0], g["betas"][1], g["eps"],
                                    g["weight_decay"])
             self._engine(dev).step(segs, rows_array(rows), self._base_seed,
-                                   events=self._step_events)
+                                   events=self._step_events, grad_scale=gs)
         return loss
+
+    def _keep_scale(self, device: torch.device, gs: torch.Tensor) -> torch.Tensor:
+        """Hold a reference to a per-device copy of the scale until the next
+        step (the kernels read it asynchronously)."""
+        self._scale_refs[device] = gs
+        return gs

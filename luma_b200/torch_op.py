@@ -51,11 +51,13 @@ def _desc_table(segs: list[Segment], device: torch.device) -> tuple[torch.Tensor
 def step(params: list[torch.Tensor], grads: list[torch.Tensor], q_m: list[torch.Tensor],
          q_w: list[torch.Tensor], slots: torch.Tensor, counters: torch.Tensor,
          row_table: torch.Tensor, param_ids: list[int], slot_ids: list[int],
-         row_bases: list[int], base_seed: int) -> None:
+         row_bases: list[int], base_seed: int,
+         grad_scale: torch.Tensor | None = None) -> None:
     """One LUMA step of every tensor in `params` (contiguous CUDA tensors on one
     device): tensor i uses state slot slot_ids[i], its step count
     counters[slot_ids[i]] (advanced by one) and the rows of its group starting
-    at row_table[row_bases[i]]; param_ids[i] keys its Philox stream."""
+    at row_table[row_bases[i]]; param_ids[i] keys its Philox stream.
+    `grad_scale` (optional float32 scalar) is fused as in ``LUMA.step``."""
     if not params:
         return
     segs = [Segment(p.view(-1), g.view(-1), m.view(-1), w.view(-1), pid, rb, sl)
@@ -72,6 +74,9 @@ def step(params: list[torch.Tensor], grads: list[torch.Tensor], q_m: list[torch.
     a.base_seed = ctypes.c_int64(int(base_seed)).value
     a.max_ctas = 0
     a.step_counters = counters.data_ptr()
+    if grad_scale is not None:
+        grad_scale = grad_scale.reshape(1).to(dtype=torch.float32)  # exact for bf16 / fp16
+    a.grad_scale = None if grad_scale is None else grad_scale.data_ptr()
     stream = torch.cuda.current_stream(params[0].device)
     _lib.check(_lib.lib().luma_step(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)),
                "luma_step")
@@ -79,5 +84,5 @@ def step(params: list[torch.Tensor], grads: list[torch.Tensor], q_m: list[torch.
 
 @step.register_fake
 def _step_fake(params, grads, q_m, q_w, slots, counters, row_table, param_ids, slot_ids,
-               row_bases, base_seed) -> None:
+               row_bases, base_seed, grad_scale=None) -> None:
     return None

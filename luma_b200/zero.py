@@ -255,10 +255,12 @@ class ZeroLUMA:
         return rows_array([step_row(self.t, self.hp["lr"], b1, b2, self.hp["eps"],
                                     self.hp["weight_decay"])])
 
-    def _step_bucket(self, b: int, grad_shard: torch.Tensor, rows, max_ctas: int) -> None:
+    def _step_bucket(self, b: int, grad_shard: torch.Tensor, rows, max_ctas: int,
+                     grad_scale: torch.Tensor | None = None) -> None:
         segs = self._engine_segments(b, grad_shard)
         self.engines[b].step(segs, rows, self.base_seed,
-                             events=self.events if b == 0 else None, max_ctas=max_ctas)
+                             events=self.events if b == 0 else None, max_ctas=max_ctas,
+                             grad_scale=grad_scale)
 
     def _gather_bucket(self, b: int) -> None:
         import torch.distributed as dist
@@ -267,13 +269,16 @@ class ZeroLUMA:
         dist.all_gather_into_tensor(self.flat[b * s:(b + 1) * s], self.flat[lo:hi], group=self.pg)
 
     @torch.no_grad()
-    def step_local(self, grad_shard: torch.Tensor) -> None:
+    def step_local(self, grad_shard: torch.Tensor,
+                   grad_scale: torch.Tensor | None = None) -> None:
         """Update this rank's pieces (two kernel launches per bucket, no communication)."""
         self._check(grad_shard)
+        if grad_scale is not None:
+            grad_scale = grad_scale.reshape(1).to(device=self.flat.device, dtype=torch.float32)
         self.t += 1
         rows = self._row()
         for b in range(self.layout.buckets):
-            self._step_bucket(b, grad_shard, rows, 0)
+            self._step_bucket(b, grad_shard, rows, 0, grad_scale)
 
     @torch.no_grad()
     def gather(self) -> None:
@@ -293,21 +298,25 @@ class ZeroLUMA:
             self._gather_bucket(b)
 
     @torch.no_grad()
-    def step(self, grad_shard: torch.Tensor) -> None:
-        """Step every bucket; bucket b's gather overlaps bucket b+1's kernels."""
+    def step(self, grad_shard: torch.Tensor, grad_scale: torch.Tensor | None = None) -> None:
+        """Step every bucket; bucket b's gather overlaps bucket b+1's kernels.
+        `grad_scale`: optional one-element device tensor fused into the step as
+        in ``LUMA.step`` (e.g. the global clip coefficient)."""
         self._check(grad_shard)
+        if grad_scale is not None:
+            grad_scale = grad_scale.reshape(1).to(device=self.flat.device, dtype=torch.float32)
         self.t += 1
         rows = self._row()
         if self.layout.world == 1:
             for b in range(self.layout.buckets):
-                self._step_bucket(b, grad_shard, rows, 0)
+                self._step_bucket(b, grad_shard, rows, 0, grad_scale)
             return
         main = torch.cuda.current_stream(self.flat.device)
         if self.peers is not None:
             # copy engines: bucket b's pushes overlap bucket b+1's kernels
             self.peers.begin(main)
             for b in range(self.layout.buckets):
-                self._step_bucket(b, grad_shard, rows, 0)
+                self._step_bucket(b, grad_shard, rows, 0, grad_scale)
                 done = torch.cuda.Event()
                 done.record(main)
                 self.peers.push(b, done)
@@ -315,7 +324,7 @@ class ZeroLUMA:
             return
         for b in range(self.layout.buckets):
             # while an earlier bucket's gather may be in flight, leave SMs to NCCL
-            self._step_bucket(b, grad_shard, rows, self.max_ctas if b > 0 else 0)
+            self._step_bucket(b, grad_shard, rows, self.max_ctas if b > 0 else 0, grad_scale)
             done = torch.cuda.Event()
             done.record(main)
             self.comm.wait_event(done)

@@ -35,3 +35,23 @@ def test_capturable_options_validated():
     assert opt.capturable and opt.capture_steps == 16
     with pytest.raises(RuntimeError, match="capturable=True"):
         LUMA(p).step_op_args()
+
+
+@pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16, torch.float16])
+def test_clip_coef_is_the_multiplier_clip_grad_norm_applies(gdt):
+    """clip_grad_norm_ stores round_to_dtype(fl32(g) * coef) with the coef
+    clip_grad_coef returns (the rounding model the fused kernels follow)."""
+    from luma_b200 import clip_grad_coef
+    gen = torch.Generator().manual_seed(3)
+    ps = [torch.nn.Parameter(torch.zeros(n)) for n in (1000, 77, 5)]
+    for p in ps:
+        p.grad_dtype = None
+        p.grad = (torch.randn(p.shape, generator=gen) * 0.5).to(gdt)
+    grads = [p.grad.clone() for p in ps]
+    norm, coef = clip_grad_coef(ps, 0.1)
+    assert all(torch.equal(p.grad, g) for p, g in zip(ps, grads))
+    ref_norm = torch.nn.utils.clip_grad_norm_(ps, 0.1)
+    assert torch.equal(norm, ref_norm)
+    assert coef.dtype == gdt and float(coef) < 1.0  # the norm's dtype follows the grads'
+    for p, g in zip(ps, grads):
+        assert torch.equal(p.grad, (g.float() * coef.float()).to(gdt))

@@ -331,3 +331,43 @@ def test_scale_max_adversarial_bit_exact(beta1):
         for i, (a, b) in enumerate(zip(pk, po)):
             assert torch.equal(a, b), f"step {step} tensor {i} ({kinds[i % len(kinds)]})"
         _assert_same_state(f"step {step}", opt, orc, pk, po, [{"params": pk}])
+
+
+@pytest.mark.parametrize("pdt,gdt", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
+                                     (torch.float32, torch.float16), (torch.bfloat16, torch.bfloat16)])
+@pytest.mark.parametrize("max_norm", [1e-3, 1e9])
+def test_fused_clip_bit_exact(pdt, gdt, max_norm):
+    """clip_grad_norm_ then step == step(grad_scale=clip_grad_coef(...)) bit
+    for bit (the reference clips before every step, bench_nanogpt.py:218-225),
+    with clipping active (max_norm 1e-3) and inactive (coefficient 1); one
+    tensor long enough for the steady loops."""
+    from luma_b200 import LUMA, clip_grad_coef
+    shapes = [(20_000_003,), (4096, 3), (1000,), (7,)]
+    gen = torch.Generator().manual_seed(21)
+    base = [(torch.randn(s, generator=gen) * 0.02).to(pdt) for s in shapes]
+    pa = [b.clone().to(DEV) for b in base]
+    pb = [b.clone().to(DEV) for b in base]
+    for t in pa + pb:
+        t.grad_dtype = None
+    torch.manual_seed(5)
+    oa = LUMA(pa, lr=1e-3)
+    torch.manual_seed(5)
+    ob = LUMA(pb, lr=1e-3)
+    for step in range(1, 4):
+        for k, s in enumerate(shapes):
+            g = (torch.randn(s, generator=gen) * 1e-2).to(gdt).to(DEV)
+            pa[k].grad = g.clone()
+            pb[k].grad = g.clone()
+        torch.nn.utils.clip_grad_norm_(pa, max_norm)
+        oa.step()
+        gb = [p.grad.clone() for p in pb]
+        _, coef = clip_grad_coef(pb, max_norm)
+        ob.step(grad_scale=coef)
+        for k in range(len(shapes)):
+            assert torch.equal(pb[k].grad, gb[k]), "grads must not be modified"
+            assert torch.equal(pa[k], pb[k]), f"step {step} param {k}: {(pa[k] != pb[k]).sum().item()} differ"
+            sa, sb = oa.state[pa[k]], ob.state[pb[k]]
+            assert torch.equal(sa["Q_m"], sb["Q_m"]) and torch.equal(sa["Q_w"], sb["Q_w"])
+        da, db = oa.state_dict()["state"], ob.state_dict()["state"]
+        for k in da:
+            assert (da[k]["S_m"], da[k]["S_v"]) == (db[k]["S_m"], db[k]["S_v"])
