@@ -397,7 +397,8 @@ def run_zero(args, rank, world, local_rank):
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     max_ctas = max(1, sms - args.reserve_sms) if args.reserve_sms > 0 else 0
     opt = ZeroLUMA(flat, lay, rank, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
-                   base_seed=1234, max_ctas=max_ctas, gather=args.gather)
+                   base_seed=1234, max_ctas=max_ctas, gather=args.gather,
+                   copy_streams=args.copy_streams)
     for _ in range(max(args.warmup, 1)):
         opt.step(gshard)
     torch.cuda.synchronize()
@@ -539,6 +540,8 @@ def main():
                     help="N>1: gather buckets (each bucket's gather overlaps the next's kernels)")
     ap.add_argument("--reserve-sms", type=int, default=0,
                     help="N>1, NCCL gather: SMs left free for NCCL while a gather is in flight")
+    ap.add_argument("--copy-streams", type=int, default=1,
+                    help="N>1, copy gather: streams the peer pushes are spread over (0: one per peer)")
     ap.add_argument("--gather", default="copy", choices=["nccl", "copy"],
                     help="N>1: post-step all-gather by NCCL or by copy-engine pushes over CUDA IPC")
     args = ap.parse_args()

@@ -125,7 +125,8 @@ class PeerGather:
     copies this rank's piece of bucket b into every peer after ``event``.
     """
 
-    def __init__(self, flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None):
+    def __init__(self, flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None,
+                 copy_streams: int = 1):
         import torch.distributed as dist
 
         from . import _lib
@@ -147,7 +148,12 @@ class PeerGather:
             self.peer_ptr[p] = base + o
         dev = flat.device
         self.comm = torch.cuda.Stream(device=dev)
-        self.streams = {p: torch.cuda.Stream(device=dev) for p in self.peer_ptr}
+        # copy streams; peers are assigned round-robin, starting after this
+        # rank so that ranks do not all target the same peer first
+        peers = [(rank + k) % layout.world for k in range(1, layout.world)]
+        n_st = max(1, min(copy_streams if copy_streams > 0 else len(peers), len(peers)))
+        self.copy_streams = [torch.cuda.Stream(device=dev) for _ in range(n_st)]
+        self.streams = {p: self.copy_streams[k % n_st] for k, p in enumerate(peers)}
         self.token = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def _barrier(self) -> None:
@@ -159,7 +165,7 @@ class PeerGather:
         """Barrier after everything queued on `main` so far (all ranks)."""
         self.comm.wait_stream(main)
         self._barrier()
-        for st in self.streams.values():
+        for st in self.copy_streams:
             st.wait_stream(self.comm)
 
     def push(self, bucket: int, ready: torch.cuda.Event) -> None:
@@ -167,13 +173,14 @@ class PeerGather:
         es = self.flat.element_size()
         src = self.flat.data_ptr() + lo * es
         nbytes = (hi - lo) * es
-        for p, st in self.streams.items():
+        for st in self.copy_streams:
             st.wait_event(ready)
+        for p, st in self.streams.items():
             self._lib.copy_async(self.peer_ptr[p] + lo * es, src, nbytes, st)
 
     def finish(self, main: torch.cuda.Stream) -> None:
         """Barrier after every push; `main` then sees the full replica."""
-        for st in self.streams.values():
+        for st in self.copy_streams:
             self.comm.wait_stream(st)
         self._barrier()
         main.wait_stream(self.comm)
@@ -198,7 +205,8 @@ class ZeroLUMA:
     def __init__(self, flat_param: torch.Tensor, layout: FlatLayout, rank: int,
                  lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01, base_seed: int | None = None,
-                 process_group=None, max_ctas: int = 0, gather: str = "nccl"):
+                 process_group=None, max_ctas: int = 0, gather: str = "nccl",
+                 copy_streams: int = 1):
         if flat_param.dim() != 1 or flat_param.numel() != layout.total:
             raise ValueError(f"flat_param must be 1-D with {layout.total} elements")
         if flat_param.dtype not in (torch.float32, torch.bfloat16):
@@ -227,7 +235,7 @@ class ZeroLUMA:
         if gather not in ("nccl", "copy"):
             raise ValueError(f"gather must be 'nccl' or 'copy', got {gather!r}")
         self.gather_mode = gather
-        self.peers = PeerGather(flat_param, layout, rank, process_group) \
+        self.peers = PeerGather(flat_param, layout, rank, process_group, copy_streams) \
             if gather == "copy" and layout.world > 1 else None
         self.t = 0
         self.events = None  # optional (ev0, ev1, ev2) cudaEvent_t handles for bucket 0 (timing)
