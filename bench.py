@@ -488,7 +488,7 @@ def run_zero(args, rank, world, local_rank):
         "overlap_saving_ms": round(ms_local + ms_gather - ms_step, 3),
         "step_only_gparams": round(n_params / (ms_local * 1e-3) / 1e9, 3),
         "shard_params": lay.shard, "buckets": lay.buckets, "max_ctas": max_ctas,
-        "gather": args.gather,
+        "gather": opt.gather_mode,
         "bytes_per_param": p1b + p2b, "pass2_bytes_per_param": p2b,
         "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<false>+<true> (local step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -542,7 +542,7 @@ def main():
                     help="N>1, NCCL gather: SMs left free for NCCL while a gather is in flight")
     ap.add_argument("--copy-streams", type=int, default=1,
                     help="N>1, copy gather: streams the peer pushes are spread over (0: one per peer)")
-    ap.add_argument("--gather", default="copy", choices=["nccl", "copy"],
+    ap.add_argument("--gather", default="auto", choices=["auto", "nccl", "copy"],
                     help="N>1: post-step all-gather by NCCL or by copy-engine pushes over CUDA IPC")
     args = ap.parse_args()
 
@@ -578,7 +578,9 @@ def main():
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
                                              timeout=datetime.timedelta(seconds=300))
         res = run_zero(args, rank, world, local_rank)
-        how = "copy-engine pushes over CUDA IPC" if args.gather == "copy" else "NCCL"
+        from luma_b200.zero import auto_gather
+        mode = auto_gather(world) if args.gather == "auto" else args.gather
+        how = "copy-engine pushes over CUDA IPC" if mode == "copy" else "NCCL"
         config_out["parallelism"] = (f"zero1-dp{world} (flat shards, per-shard scales, "
                                      f"bf16 all-gather: {how})")
         scaling = "strong"

@@ -117,6 +117,14 @@ def flat_views(flat: torch.Tensor, layout: FlatLayout, shapes) -> list[torch.Ten
     return [flat[s:s + n].view(shape) for shape, n, s in zip(shapes, layout.numels, layout.starts)]
 
 
+def auto_gather(world: int) -> str:
+    """Gather measured faster on B200 (Llama-3-8B, 8 buckets): copy engines up
+    to 4 ranks (2: 196 vs 145 Gparams/s, 4: 354 vs 212), NCCL at 8 (304 vs
+    291), where every rank receives 7/8 of the params and NCCL's transfer
+    rate (642 GB/s per rank) beats the copy engines' (580)."""
+    return "copy" if world <= 4 else "nccl"
+
+
 class PeerGather:
     """Copy-engine all-gather of the flat buffer's bucket pieces over CUDA IPC.
 
@@ -232,8 +240,10 @@ class ZeroLUMA:
             eng.ensure_slots(max(1, len(segs)))
             self.engines.append(eng)
         self.comm = torch.cuda.Stream(device=dev)
-        if gather not in ("nccl", "copy"):
-            raise ValueError(f"gather must be 'nccl' or 'copy', got {gather!r}")
+        if gather not in ("nccl", "copy", "auto"):
+            raise ValueError(f"gather must be 'nccl', 'copy' or 'auto', got {gather!r}")
+        if gather == "auto":
+            gather = auto_gather(layout.world)
         self.gather_mode = gather
         self.peers = PeerGather(flat_param, layout, rank, process_group, copy_streams) \
             if gather == "copy" and layout.world > 1 else None

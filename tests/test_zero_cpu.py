@@ -108,3 +108,8 @@ def test_gather_rebuilds_params_gloo(world, buckets):
         assert p.exitcode == 0
     results = dict(q.get(timeout=10) for _ in range(world))
     assert all(results.values()), results
+
+
+def test_auto_gather_policy():
+    from luma_b200.zero import auto_gather
+    assert [auto_gather(w) for w in (1, 2, 4, 8)] == ["copy", "copy", "copy", "nccl"]
