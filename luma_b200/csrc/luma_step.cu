@@ -515,11 +515,6 @@ __device__ __forceinline__ void load8_codes(const int16_t* base, int64_t e0, int
   }
 }
 
-__device__ __forceinline__ void load8_f32_plain(const float* base, int64_t e0, int n, bool vec,
-                                                float (&x)[8]) {
-  load8<LUMA_F32>(base, e0, n, vec, x);
-}
-
 template <int DT>
 __device__ __forceinline__ void store8(void* base, int64_t e0, int n, bool vec, const float (&x)[8]) {
   if (DT == LUMA_F32) {
@@ -546,20 +541,6 @@ __device__ __forceinline__ void store8(void* base, int64_t e0, int n, bool vec, 
       for (int j = 0; j < 8; ++j)
         if (j < n) p[j] = h[j];
     }
-  }
-}
-
-__device__ __forceinline__ void store8_codes(int16_t* base, int64_t e0, int n, bool vec,
-                                             const uint16_t (&q)[8]) {
-  uint16_t* p = reinterpret_cast<uint16_t*>(base) + e0;
-  if (vec) {
-    uint4 a;
-    memcpy(&a, q, 16);
-    __stcs(reinterpret_cast<uint4*>(p), a);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j < n) p[j] = q[j];
   }
 }
 
@@ -813,17 +794,6 @@ __device__ __forceinline__ void load2(const void* base, int64_t e, bool both, bo
       x0 = __half2float(__ushort_as_half((unsigned short)h0));
       x1 = __half2float(__ushort_as_half((unsigned short)h1));
     }
-  }
-}
-
-__device__ __forceinline__ void load2_codes(const int16_t* base, int64_t e, bool both, bool vec,
-                                            uint32_t& q0, uint32_t& q1) {
-  const uint16_t* p = reinterpret_cast<const uint16_t*>(base) + e;
-  if (vec) {
-    const uint32_t a = __ldcs(reinterpret_cast<const unsigned int*>(p));
-    q0 = a & 0xFFFFu; q1 = a >> 16;
-  } else {
-    q0 = p[0]; q1 = both ? p[1] : 0u;
   }
 }
 
@@ -1303,7 +1273,7 @@ __device__ __forceinline__ void pass2_segment(const SegShared& s, const Consts& 
 // constants read from the segment state in shared memory.  (Inlined: an
 // out-of-line version per dtype pair measured 3% slower.)
 template <int PD, int GD>
-__device__ __forceinline__ void pass2_segment_nl(bool use_lut, uint32_t k0, uint32_t k1, bool vec2,
+__device__ __forceinline__ void pass2_segment_from_shared(bool use_lut, uint32_t k0, uint32_t k1, bool vec2,
                                               int64_t p_lo, int64_t p_hi) {
   Consts c;
   fill_consts(g_seg, true, c);
@@ -1317,15 +1287,15 @@ __device__ __forceinline__ void dispatch_pass2(const SegShared& s, const float* 
   const LumaTensorDesc& d = s.d;
   if (d.param_dtype == LUMA_F32) {
     switch (d.grad_dtype) {
-      case LUMA_F32: pass2_segment_nl<LUMA_F32, LUMA_F32>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
-      case LUMA_BF16: pass2_segment_nl<LUMA_F32, LUMA_BF16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
-      default: pass2_segment_nl<LUMA_F32, LUMA_F16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_F32: pass2_segment_from_shared<LUMA_F32, LUMA_F32>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_segment_from_shared<LUMA_F32, LUMA_BF16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_segment_from_shared<LUMA_F32, LUMA_F16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
     }
   } else {
     switch (d.grad_dtype) {
-      case LUMA_F32: pass2_segment_nl<LUMA_BF16, LUMA_F32>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
-      case LUMA_BF16: pass2_segment_nl<LUMA_BF16, LUMA_BF16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
-      default: pass2_segment_nl<LUMA_BF16, LUMA_F16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_F32: pass2_segment_from_shared<LUMA_BF16, LUMA_F32>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      case LUMA_BF16: pass2_segment_from_shared<LUMA_BF16, LUMA_BF16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
+      default: pass2_segment_from_shared<LUMA_BF16, LUMA_F16>(lut != nullptr, k0, k1, vec2, p_lo, p_hi); break;
     }
   }
 }
