@@ -73,6 +73,15 @@ def ragged_shapes(n=10_000, seed=0):
     return [(max(1, int(round(2 ** rng.uniform(0, 20)))),) for _ in range(n)]
 
 
+def llama3_70b_shapes():
+    d, kv, ffn, vocab, layers = 8192, 1024, 28672, 128256, 80
+    shapes = [(vocab, d)]
+    for _ in range(layers):
+        shapes += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
+    shapes += [(d,), (vocab, d)]
+    return shapes
+
+
 def llama_layer_shapes():
     d, kv, ffn = 4096, 1024, 14336
     return [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
@@ -85,6 +94,9 @@ def cpu21m_shapes():
 CONFIGS = {
     "llama8b": dict(shapes=llama3_8b_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
                     gscale=1e-3, name="Llama-3-8B shapes (291 tensors), bf16 params, bf16 grads"),
+    "llama70b": dict(shapes=llama3_70b_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
+                     gscale=1e-3, name="Llama-3-70B shapes (723 tensors), bf16 params, bf16 grads "
+                     "(N>1: params sharded, buckets gathered into staging buffers)"),
     "llama_layer": dict(shapes=llama_layer_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
                         gscale=1e-3, name="one Llama-3-8B decoder layer (9 tensors, 218,112,000 "
                         "params), bf16 params, bf16 grads (profiling case)"),
@@ -388,9 +400,13 @@ def run_zero(args, rank, world, local_rank):
     shapes = cfg["shapes"]()
     numels = [numel(s) for s in shapes]
     n_params = sum(numels)
-    lay = plan_layout(numels, world, args.buckets)
+    # A full bf16 replica plus the shard state must fit in HBM; otherwise the
+    # params stay sharded and every bucket is gathered into a staging buffer.
+    replica = args.config != "llama70b"
+    buckets = args.buckets if replica else max(args.buckets, 32)
+    lay = plan_layout(numels, world, buckets)
     gen = torch.Generator(device=device).manual_seed(0)
-    flat = torch.empty(lay.total, dtype=cfg["pdt"], device=device)
+    flat = torch.empty(lay.total if replica else lay.shard, dtype=cfg["pdt"], device=device)
     flat.normal_(0.0, 0.02, generator=gen)
     gshard = torch.empty(lay.shard, dtype=cfg["gdt"], device=device)
     gshard.normal_(0.0, cfg["gscale"], generator=gen)
@@ -398,7 +414,7 @@ def run_zero(args, rank, world, local_rank):
     max_ctas = max(1, sms - args.reserve_sms) if args.reserve_sms > 0 else 0
     opt = ZeroLUMA(flat, lay, rank, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                    base_seed=1234, max_ctas=max_ctas, gather=args.gather,
-                   copy_streams=args.copy_streams)
+                   copy_streams=args.copy_streams, replica=replica)
     for _ in range(max(args.warmup, 1)):
         opt.step(gshard)
     torch.cuda.synchronize()
@@ -488,7 +504,7 @@ def run_zero(args, rank, world, local_rank):
         "overlap_saving_ms": round(ms_local + ms_gather - ms_step, 3),
         "step_only_gparams": round(n_params / (ms_local * 1e-3) / 1e9, 3),
         "shard_params": lay.shard, "buckets": lay.buckets, "max_ctas": max_ctas,
-        "gather": opt.gather_mode,
+        "gather": opt.gather_mode, "replica": replica,
         "bytes_per_param": p1b + p2b, "pass2_bytes_per_param": p2b,
         "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<false>+<true> (local step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -521,7 +537,7 @@ def result_line(args, res, world, scaling, dtype, config_out):
             "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
             "gpu_launches": res["gpu_launches"]}
     for key in ("local_step_ms", "allgather_ms", "allgather_gbs_per_rank", "overlap_saving_ms",
-                "step_only_gparams", "shard_params", "buckets", "max_ctas", "gather"):
+                "step_only_gparams", "shard_params", "buckets", "max_ctas", "gather", "replica"):
         if key in res:
             line[key] = res[key]
     return line
@@ -585,6 +601,9 @@ def main():
                                      f"bf16 all-gather: {how})")
         scaling = "strong"
     else:
+        if args.config == "llama70b":
+            raise SystemExit("llama70b: 141 GB of bf16 params do not fit one GPU with their "
+                             "state; run it on 8 GPUs (params sharded)")
         res = run_luma(args, rank, world, local_rank)
         scaling = "weak"
     if rank == 0:

@@ -125,6 +125,19 @@ def auto_gather(world: int) -> str:
     return "copy" if world <= 4 else "nccl"
 
 
+def gather_bucket_into(staging: torch.Tensor, shard: torch.Tensor, layout: FlatLayout,
+                       bucket: int, group=None) -> torch.Tensor:
+    """Sharded-params mode: all-gather bucket `bucket` of every rank's shard
+    (``shard`` holds this rank's pieces back to back) into `staging`
+    (``layout.span`` elements: rank r's piece at ``r * layout.piece``), which
+    then holds flat positions ``[bucket * span, (bucket + 1) * span)``."""
+    import torch.distributed as dist
+    p = layout.piece
+    view = staging[:layout.span]
+    dist.all_gather_into_tensor(view, shard[bucket * p:(bucket + 1) * p], group=group)
+    return view
+
+
 class PeerGather:
     """Copy-engine all-gather of the flat buffer's bucket pieces over CUDA IPC.
 
@@ -202,21 +215,33 @@ class PeerGather:
 
 
 class ZeroLUMA:
-    """LUMA step over this rank's pieces, then per-bucket NCCL all-gathers.
+    """LUMA step over this rank's pieces, then per-bucket all-gathers.
 
     ``flat_param``: the full flat param buffer (fp32 or bf16), every rank a
     replica, laid out by ``layout`` (``plan_layout`` / ``flat_views``).
     ``step(grad_shard)`` takes this rank's grads, ``layout.shard`` elements:
     its piece of bucket 0, then of bucket 1, and so on.
+
+    ``replica=False`` is the mode for models whose full replica does not fit
+    next to the shard state (Llama-3-70B on 8 GPUs: 141 GB of bf16 params):
+    ``flat_param`` then holds only this rank's pieces (``layout.shard``
+    elements, the grads' layout), and each bucket is all-gathered (NCCL) into
+    one of ``staging`` rotating buffers of ``layout.span`` elements;
+    ``consumer(bucket, view)``, called with the gather's stream current, gets
+    each gathered bucket before its buffer is reused.
     """
 
     def __init__(self, flat_param: torch.Tensor, layout: FlatLayout, rank: int,
                  lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01, base_seed: int | None = None,
                  process_group=None, max_ctas: int = 0, gather: str = "nccl",
-                 copy_streams: int = 1):
-        if flat_param.dim() != 1 or flat_param.numel() != layout.total:
-            raise ValueError(f"flat_param must be 1-D with {layout.total} elements")
+                 copy_streams: int = 1, replica: bool = True, staging: int = 2,
+                 consumer=None):
+        want = layout.total if replica else layout.shard
+        if flat_param.dim() != 1 or flat_param.numel() != want:
+            raise ValueError(f"flat_param must be 1-D with {want} elements")
+        if staging < 1:
+            raise ValueError("staging must be >= 1")
         if flat_param.dtype not in (torch.float32, torch.bfloat16):
             raise ValueError("flat_param must be float32 or bfloat16")
         if not flat_param.is_cuda:
@@ -244,6 +269,14 @@ class ZeroLUMA:
             raise ValueError(f"gather must be 'nccl', 'copy' or 'auto', got {gather!r}")
         if gather == "auto":
             gather = auto_gather(layout.world)
+        self.replica = replica
+        self.consumer = consumer
+        self.staging = []
+        if not replica:
+            gather = "nccl"  # the gathered buckets go to local staging buffers
+            if layout.world > 1:
+                self.staging = [torch.empty(layout.span, dtype=flat_param.dtype, device=dev)
+                                for _ in range(staging)]
         self.gather_mode = gather
         self.peers = PeerGather(flat_param, layout, rank, process_group, copy_streams) \
             if gather == "copy" and layout.world > 1 else None
@@ -258,7 +291,8 @@ class ZeroLUMA:
         out = []
         for k, sg in enumerate(self.bucket_segments[b]):
             lo = sg.local
-            out.append(Segment(self.flat[sg.flat:sg.flat + sg.length],
+            pos = sg.flat if self.replica else sg.local
+            out.append(Segment(self.flat[pos:pos + sg.length],
                                grad_shard[lo:lo + sg.length],
                                self.q_m[lo:lo + sg.length], self.q_w[lo:lo + sg.length],
                                param_id=sg.tensor, row=0, slot=k, rng_offset=sg.offset))
@@ -282,6 +316,12 @@ class ZeroLUMA:
 
     def _gather_bucket(self, b: int) -> None:
         import torch.distributed as dist
+        if not self.replica:
+            view = gather_bucket_into(self.staging[b % len(self.staging)], self.flat, self.layout,
+                                      b, self.pg)
+            if self.consumer is not None:
+                self.consumer(b, view)
+            return
         s = self.layout.span
         lo, hi = self.layout.owned(self.rank, b)
         dist.all_gather_into_tensor(self.flat[b * s:(b + 1) * s], self.flat[lo:hi], group=self.pg)

@@ -52,10 +52,26 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
         for v, s in zip(flat_views(flat, lay, SHAPES), SHAPES):
             v.copy_((torch.randn(s, generator=gen) * 0.02).to(pdt))
         segs = shard_segments(lay, rank)
-        opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, max_ctas=100,
-                       gather=gather)
+        sharded = gather == "sharded"
+        if sharded:
+            # params held as this rank's pieces only; buckets gathered into staging
+            full = flat
+            flat = torch.cat([full[slice(*lay.owned(rank, b))] for b in range(lay.buckets)])
+            gathered = torch.zeros_like(full)
+
+            def consumer(b, view):
+                gathered[b * lay.span:(b + 1) * lay.span].copy_(view)
+
+            opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, replica=False,
+                           consumer=consumer)
+        else:
+            opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, max_ctas=100,
+                           gather=gather)
+
+        def pos(sg):
+            return sg.local if sharded else sg.flat
         # oracle: every local segment as its own tensor
-        oparams = [flat[sg.flat:sg.flat + sg.length].clone() for sg in segs]
+        oparams = [flat[pos(sg):pos(sg) + sg.length].clone() for sg in segs]
         for p in oparams:
             p.grad_dtype = None
 
@@ -76,7 +92,7 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
             torch.cuda.synchronize()
             for k, sg in enumerate(segs):
                 lo = sg.local
-                if not torch.equal(flat[sg.flat:sg.flat + sg.length], oparams[k]):
+                if not torch.equal(flat[pos(sg):pos(sg) + sg.length], oparams[k]):
                     msgs.append(f"t={t} seg {k}: params differ")
                 ost = orc.state[id(oparams[k])]
                 if not torch.equal(opt.q_m[lo:lo + sg.length], ost["Q_m"]):
@@ -88,10 +104,16 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
                 if (S_m, S_v) != (ost["S_m"], ost["S_v"]):
                     msgs.append(f"t={t} seg {k}: scales differ")
             # replicas identical after the gather
-            other = torch.empty_like(flat)
-            dist.broadcast(other.copy_(flat), src=0)
-            if not torch.equal(other, flat):
+            rep = gathered if sharded else flat
+            other = torch.empty_like(rep)
+            dist.broadcast(other.copy_(rep), src=0)
+            if not torch.equal(other, rep):
                 msgs.append(f"t={t}: gathered replicas differ")
+            if sharded:
+                for b in range(lay.buckets):
+                    lo, hi = lay.owned(rank, b)
+                    if not torch.equal(gathered[lo:hi], flat[b * lay.piece:(b + 1) * lay.piece]):
+                        msgs.append(f"t={t}: gathered bucket {b} lacks this rank's piece")
         opt.close()
         out_q.put((rank, msgs))
     except Exception as exc:  # noqa: BLE001
@@ -102,7 +124,7 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
 
 @pytest.mark.parametrize("pdt_name,buckets,gather", [
     ("bfloat16", 1, "nccl"), ("float32", 1, "nccl"), ("bfloat16", 3, "nccl"),
-    ("bfloat16", 3, "copy"), ("float32", 1, "copy")])
+    ("bfloat16", 3, "copy"), ("float32", 1, "copy"), ("bfloat16", 3, "sharded")])
 def test_zero_sharded_step_two_gpus(pdt_name, buckets, gather):
     world = 2
     ctx = mp.get_context("spawn")

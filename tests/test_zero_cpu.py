@@ -113,3 +113,48 @@ def test_gather_rebuilds_params_gloo(world, buckets):
 def test_auto_gather_policy():
     from luma_b200.zero import auto_gather
     assert [auto_gather(w) for w in (1, 2, 4, 8)] == ["copy", "copy", "copy", "nccl"]
+
+
+def _staged_worker(rank, world, port, numels, buckets, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from luma_b200.zero import gather_bucket_into
+        lay = plan_layout(numels, world, buckets)
+        # sharded params: this rank's pieces back to back (the grads' layout)
+        shard = torch.full((lay.shard,), -1.0)
+        for sg in shard_segments(lay, rank):
+            shard[sg.local:sg.local + sg.length] = torch.arange(sg.length, dtype=torch.float32) + \
+                1000.0 * sg.tensor + sg.offset
+        staging = [torch.empty(lay.span) for _ in range(2)]
+        full = torch.full((lay.total,), -1.0)
+        for b in range(buckets):  # rotating staging buffers, consumed bucket by bucket
+            view = gather_bucket_into(staging[b % 2], shard, lay, b)
+            full[b * lay.span:(b + 1) * lay.span] = view
+        ok = True
+        for t, (n, s) in enumerate(zip(lay.numels, lay.starts)):
+            want = torch.arange(n, dtype=torch.float32) + 1000.0 * t
+            ok &= bool(torch.equal(full[s:s + n], want))
+        out_q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,buckets", [(2, 1), (2, 4), (3, 3)])
+def test_staged_gather_rebuilds_buckets_gloo(world, buckets):
+    """Sharded-params mode: each bucket gathered into a rotating staging buffer
+    holds the flat positions of that bucket."""
+    numels = [37, 1024, 5, 999, 64]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_staged_worker, args=(r, world, port, numels, buckets, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert all(results.values()), results
