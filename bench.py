@@ -45,7 +45,7 @@ FALLBACK_HBM_GBS = 6650.0
 
 
 # ---------------------------------------------------------------------------
-# workloads (SURVEY-listed synthetic configs)
+# workloads (synthetic configs with the reference benchmarks' shapes)
 # ---------------------------------------------------------------------------
 
 def llama3_8b_shapes():
