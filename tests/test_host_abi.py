@@ -139,3 +139,23 @@ def test_desc_table_octets_and_alignment():
     assert total == 18
     assert list(table["vec_ok"]) == [1, 1, 0, 1]  # element offset 129 breaks 16-byte alignment
     assert list(table["param_dtype"]) == [0] * 4 and list(table["slot"]) == [0, 1, 2, 3]
+
+
+def test_new_entry_points_reject_bad_arguments_without_gpu():
+    h = _lib.lib()
+    assert h.luma_error_flags(None, 0) == _lib.LUMA_ERR_INVALID
+    assert h.luma_arith_selfcheck(16, 0, None, None) == _lib.LUMA_ERR_INVALID
+    assert h.luma_ipc_export(None, None, None) == _lib.LUMA_ERR_INVALID
+    assert h.luma_ipc_open(None, None) == _lib.LUMA_ERR_INVALID
+    assert h.luma_ipc_close(None) == _lib.LUMA_ERR_INVALID
+    assert h.luma_copy_async(None, None, 0, None) == _lib.LUMA_OK  # nothing to copy
+    assert h.luma_copy_async(None, None, 16, None) == _lib.LUMA_ERR_INVALID
+    assert b"NULL" in h.luma_last_error()
+
+
+def test_step_args_carry_capturable_and_scale_fields():
+    a = _lib.LumaStepArgs()
+    names = [f for f, _ in _lib.LumaStepArgs._fields_]
+    assert names[-2:] == ["step_counters", "grad_scale"]
+    assert a.step_counters is None and a.grad_scale is None
+    assert ctypes.sizeof(a) == 96
