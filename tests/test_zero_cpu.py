@@ -158,3 +158,18 @@ def test_staged_gather_rebuilds_buckets_gloo(world, buckets):
         assert p.exitcode == 0
     results = dict(q.get(timeout=10) for _ in range(world))
     assert all(results.values()), results
+
+
+def test_zero_luma_validates_buffers_on_cpu():
+    from luma_b200.zero import ZeroLUMA
+    lay = plan_layout([100, 37], 2, 2)
+    with pytest.raises(ValueError, match="elements"):
+        ZeroLUMA(torch.zeros(lay.total + 1, dtype=torch.bfloat16), lay, 0)
+    with pytest.raises(ValueError, match="elements"):  # sharded mode holds lay.shard elements
+        ZeroLUMA(torch.zeros(lay.total, dtype=torch.bfloat16), lay, 0, replica=False)
+    with pytest.raises(ValueError, match="staging"):
+        ZeroLUMA(torch.zeros(lay.shard, dtype=torch.bfloat16), lay, 0, replica=False, staging=0)
+    with pytest.raises(ValueError, match="float32 or bfloat16"):
+        ZeroLUMA(torch.zeros(lay.total, dtype=torch.float16), lay, 0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ZeroLUMA(torch.zeros(lay.total, dtype=torch.bfloat16), lay, 0)
