@@ -543,6 +543,58 @@ def result_line(args, res, world, scaling, dtype, config_out):
     return line
 
 
+def vs_reference_triton(args) -> dict:
+    """Opt-in comparison (--vs-triton, one GPU): this backend and the reference's
+    own Triton backend (installed unmodified into baseline/_ref) stepping the
+    same fp32 params and fp32 grads of the config's shapes, CUDA events over
+    the timed steps.  The reference takes fp32 params only, and its kernels
+    receive param_id as a plain int that Triton specialises to a constant for 0
+    and 1 (then `param_id.to(tl.int64)` fails to compile), so two gradless
+    tensors come first and the stepped tensors have ids >= 2."""
+    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "luma_optimizer")):
+        return {"impl": "reference-triton", "unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, ref_dir)
+    from luma_optimizer import LUMA as RefLUMA
+
+    from luma_b200 import LUMA
+    shapes = CONFIGS[args.config]["shapes"]()
+    n = sum(numel(s) for s in shapes)
+
+    def make():
+        g = torch.Generator(device="cuda").manual_seed(0)
+        ps = []
+        for s in shapes:
+            p = torch.empty(s, device="cuda")
+            p.normal_(0.0, 0.02, generator=g)
+            gr = torch.empty(s, device="cuda")
+            gr.normal_(0.0, 1e-3, generator=g)
+            p.grad = gr
+            ps.append(p)
+        return ps
+
+    def timeit(opt):
+        for _ in range(max(args.warmup, 3)):
+            opt.step()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            opt.step()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / args.steps
+
+    ours = timeit(LUMA(make(), lr=1e-3))
+    torch.cuda.empty_cache()
+    dummies = [torch.zeros(8, device="cuda") for _ in range(2)]
+    ref = timeit(RefLUMA(dummies + make(), lr=1e-3, backend="triton"))
+    return {"impl": "luma_b200 vs reference-triton", "config": args.config, "params": n,
+            "dtype": "fp32 params, fp32 grads", "steps": args.steps,
+            "luma_b200_ms": round(ours, 4), "reference_triton_ms": round(ref, 4),
+            "speedup": round(ref / ours, 2)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -560,7 +612,13 @@ def main():
                     help="N>1, copy gather: streams the peer pushes are spread over (0: one per peer)")
     ap.add_argument("--gather", default="auto", choices=["auto", "nccl", "copy"],
                     help="N>1: post-step all-gather by NCCL or by copy-engine pushes over CUDA IPC")
+    ap.add_argument("--vs-triton", action="store_true",
+                    help="one GPU: also time the reference's Triton backend (baseline/_ref) on the "
+                         "config's shapes in fp32 and print a comparison line")
     args = ap.parse_args()
+    if args.vs_triton:
+        print(json.dumps(vs_reference_triton(args)))
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
