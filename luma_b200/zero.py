@@ -125,6 +125,19 @@ def auto_gather(world: int) -> str:
     return "copy" if world <= 4 else "nccl"
 
 
+def push_order(rank: int, world: int, copy_streams: int) -> list[tuple[int, int]]:
+    """(peer, stream index) in the order this rank pushes to its peers: rank+1,
+    rank+2, ... (mod world), so that the ranks start on different peers (with
+    every rank pushing to peer 0 first the 4-GPU gather ran at half the rate);
+    peers are dealt round-robin over min(copy_streams, world-1) streams
+    (copy_streams <= 0: one stream per peer)."""
+    peers = [(rank + k) % world for k in range(1, world)]
+    if not peers:
+        return []
+    n_st = max(1, min(copy_streams if copy_streams > 0 else len(peers), len(peers)))
+    return [(p, k % n_st) for k, p in enumerate(peers)]
+
+
 def gather_bucket_into(staging: torch.Tensor, shard: torch.Tensor, layout: FlatLayout,
                        bucket: int, group=None) -> torch.Tensor:
     """Sharded-params mode: all-gather bucket `bucket` of every rank's shard
@@ -169,12 +182,10 @@ class PeerGather:
             self.peer_ptr[p] = base + o
         dev = flat.device
         self.comm = torch.cuda.Stream(device=dev)
-        # copy streams; peers are assigned round-robin, starting after this
-        # rank so that ranks do not all target the same peer first
-        peers = [(rank + k) % layout.world for k in range(1, layout.world)]
-        n_st = max(1, min(copy_streams if copy_streams > 0 else len(peers), len(peers)))
+        order = push_order(rank, layout.world, copy_streams)
+        n_st = 1 + max(k for _, k in order)
         self.copy_streams = [torch.cuda.Stream(device=dev) for _ in range(n_st)]
-        self.streams = {p: self.copy_streams[k % n_st] for k, p in enumerate(peers)}
+        self.streams = {p: self.copy_streams[k] for p, k in order}
         self.token = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def _barrier(self) -> None:

@@ -173,3 +173,21 @@ def test_zero_luma_validates_buffers_on_cpu():
         ZeroLUMA(torch.zeros(lay.total, dtype=torch.float16), lay, 0)
     with pytest.raises(RuntimeError, match="CUDA"):
         ZeroLUMA(torch.zeros(lay.total, dtype=torch.bfloat16), lay, 0)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("streams", [1, 2, 0])
+def test_push_order_rotates_and_covers_peers(world, streams):
+    from luma_b200.zero import push_order
+    firsts = []
+    for r in range(world):
+        order = push_order(r, world, streams)
+        peers = [p for p, _ in order]
+        assert sorted(peers) == [p for p in range(world) if p != r]
+        assert peers[0] == (r + 1) % world
+        n_st = len({k for _, k in order})
+        assert n_st == (world - 1 if streams <= 0 else min(streams, world - 1))
+        firsts.append(peers[0])
+    # at every position of the order, the ranks target distinct peers (a permutation)
+    for pos in range(world - 1):
+        assert len({push_order(r, world, streams)[pos][0] for r in range(world)}) == world
