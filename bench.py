@@ -14,12 +14,19 @@ Printed (rank 0, one JSON line): step throughput in Gparams/s (``value``),
 achieved HBM bandwidth against the algorithmic bytes per param, the roofline
 of the dominant kernel (pass 2) from per-pass CUDA events, ``e2e`` through the
 public API with grads copied from pinned host memory every step, the
-reference CPU implementation (oracle restatement of the reference's PyTorch
-backend) timed on this host's cores, and the SM clocks sampled during timing.
+reference's own PyTorch backend (the unmodified package installed in
+``baseline/_ref``) timed on this host's cores, the reference's own GPU kernels
+(its Triton backend) beside this backend on the same shapes, and the SM
+clocks sampled during timing.
 
-``--impl reference`` times the reference algorithm on the host CPU cores
-(the oracle restatement; the reference itself is a Python package that is
-not present on the GPU host) on a bounded sample of the same workload.
+``--impl reference`` times the reference's PyTorch backend on the host CPU
+cores (``luma_optimizer.LUMA(backend="pytorch")`` from ``baseline/_ref``,
+drawing its own uniforms every step; the oracle restatement only when that
+install is absent) on a bounded sample of the same workload.
+
+``--config nanogpt`` runs the end-to-end training configuration instead: GPT-2
+small on uniform-random token ids, batch 12 x 1024, LUMA and AdamW trained on
+the same batches from the same init.
 """
 
 from __future__ import annotations
@@ -92,6 +99,9 @@ def cpu21m_shapes():
 
 
 CONFIGS = {
+    # grads: "normal" N(0, gscale); "sigma" per-tensor sigma log-uniform in
+    # [1e-4, 1e-1]; "stress" N(0, gscale) with ~10% all-zero tensors and, in
+    # the others, 1% of elements at +-1e4 or +-1e-40 (BASELINE configs 1 and 3)
     "llama8b": dict(shapes=llama3_8b_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
                     gscale=1e-3, name="Llama-3-8B shapes (291 tensors), bf16 params, bf16 grads"),
     "llama70b": dict(shapes=llama3_70b_shapes, pdt=torch.bfloat16, gdt=torch.bfloat16,
@@ -102,10 +112,12 @@ CONFIGS = {
                         "params), bf16 params, bf16 grads (profiling case)"),
     "gpt2": dict(shapes=gpt2_small_shapes, pdt=torch.float32, gdt=torch.bfloat16,
                  gscale=1e-3, name="GPT-2 small shapes (148 tensors), fp32 params, bf16 grads"),
-    "ragged": dict(shapes=ragged_shapes, pdt=torch.float32, gdt=torch.float32,
-                   gscale=1e-2, name="ragged: 10,000 fp32 tensors, numel log-uniform in [1, 2^20]"),
-    "cpu21m": dict(shapes=cpu21m_shapes, pdt=torch.float32, gdt=torch.float32,
-                   gscale=1e-2, name="8 fp32 tensors, 20,971,520 params (reference CPU config)"),
+    "ragged": dict(shapes=ragged_shapes, pdt=torch.float32, gdt=torch.float32, grads="stress",
+                   gscale=1e-2, name="ragged: 10,000 fp32 tensors, numel log-uniform in [1, 2^20], "
+                   "grads N(0,1e-2) with ~10% all-zero tensors and 1% elements at +-1e4 / +-1e-40"),
+    "cpu21m": dict(shapes=cpu21m_shapes, pdt=torch.float32, gdt=torch.float32, grads="sigma",
+                   gscale=1e-2, name="8 fp32 tensors, 20,971,520 params (reference CPU config), "
+                   "grads N(0, sigma_t), sigma_t log-uniform in [1e-4, 1e-1]"),
 }
 
 
@@ -209,64 +221,101 @@ def cpu_sample_shapes(config):
     return ragged_shapes(200, seed=1), "200 ragged tensors"
 
 
-def cpu_baseline(config, steps, warmup, budget_s=20.0):
-    """Gparams/s of the reference algorithm on CPU (torch CPU kernels, all host threads)."""
-    from oracle import philox  # noqa: F401  (test infrastructure: CPU baseline leg)
-    from oracle.luma_ref import OracleLUMA
+def reference_package():
+    """The unmodified reference package installed in baseline/_ref, or None."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "luma_optimizer")):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    import luma_optimizer
+    return luma_optimizer
 
+
+def cpu_baseline(config, steps, warmup, budget_s=20.0):
+    """Gparams/s of the reference's PyTorch backend on the host CPU cores (all
+    threads): ``luma_optimizer.LUMA(backend="pytorch")`` from baseline/_ref,
+    unmodified, drawing its own uniforms every step.  Only if that install is
+    missing, the oracle restatement of the same op sequence (fresh uniforms
+    every step too).  The reference takes float32 params only
+    (optimizer.py:443-448), so bf16-param configs run with float32 params."""
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
     cfg = CONFIGS[config]
     shapes, sample = cpu_sample_shapes(config)
     g = torch.Generator().manual_seed(0)
-    params = [(torch.randn(s, generator=g) * 0.02).to(cfg["pdt"]) for s in shapes]
+    params = [torch.nn.Parameter(torch.randn(s, generator=g) * 0.02) for s in shapes]
     grads = [(torch.randn(s, generator=g) * cfg["gscale"]).to(cfg["gdt"]) for s in shapes]
     for p, gr in zip(params, grads):
         p.grad_dtype = None
         p.grad = gr
-    rand_cache = {}
+    ref = reference_package()
+    if ref is not None:
+        opt = ref.LUMA(params, lr=1e-3, backend="pytorch")
+        kind, how = "reference", "luma_optimizer.LUMA(backend='pytorch') from baseline/_ref (unmodified)"
+    else:
+        from oracle.luma_ref import OracleLUMA  # test infrastructure: CPU baseline leg only
 
-    def draws(pid, t, like):
-        if pid not in rand_cache:
-            rand_cache[pid] = (torch.rand(like.shape, generator=g), torch.rand(like.shape, generator=g))
-        return rand_cache[pid]
+        def draws(pid, t, like):
+            return torch.rand(like.shape, generator=g), torch.rand(like.shape, generator=g)
 
-    opt = OracleLUMA(params, lr=1e-3, draws=draws)
+        opt = OracleLUMA(params, lr=1e-3, draws=draws)
+        kind, how = "port", "oracle/luma_ref.py (reference op sequence; the reference install is absent)"
     n = sum(numel(s) for s in shapes)
-    for _ in range(max(warmup, 2)):
-        opt.step()
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while len(times) < steps and (not times or time.perf_counter() < t_end):
-        t0 = time.perf_counter()
-        opt.step()
-        times.append(time.perf_counter() - t0)
+    with torch.no_grad():
+        for _ in range(max(warmup, 2)):
+            opt.step()
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while len(times) < steps and (not times or time.perf_counter() < t_end):
+            t0 = time.perf_counter()
+            opt.step()
+            times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     return {"value": round(n / t / 1e9, 6), "unit": "Gparams/s", "cores": cores,
-            "kind": "port", "steps_timed": len(times),
-            "sample": f"{sample}; {cfg['pdt']} params, {cfg['gdt']} grads; median of "
-                      f"{len(times)} steps after {max(warmup, 2)} warm-up; reference "
-                      f"PyTorch-backend op sequence (oracle/luma_ref.py) on CPU tensors"}
+            "kind": kind, "steps_timed": len(times),
+            "sample": f"{sample}; fp32 params, {str(cfg['gdt']).replace('torch.', '')} grads; "
+                      f"median of {len(times)} steps after {max(warmup, 2)} warm-up; {how}"}
 
 
 # ---------------------------------------------------------------------------
 # the CUDA step
 # ---------------------------------------------------------------------------
 
-def make_workload(config, device, seed=0):
+def fill_grads(cfg, grads, gen, seed=0):
+    """Draw the config's grads in place (BASELINE.json value distributions)."""
+    import numpy as np
+    kind = cfg.get("grads", "normal")
+    rng = np.random.default_rng(seed)
+    sigmas = np.exp(rng.uniform(math.log(1e-4), math.log(1e-1), len(grads)))
+    zero = rng.random(len(grads)) < 0.10
+    for k, gr in enumerate(grads):
+        gr.normal_(0.0, float(sigmas[k]) if kind == "sigma" else cfg["gscale"], generator=gen)
+        if kind == "stress":
+            if zero[k]:
+                gr.zero_()
+                continue
+            u = torch.rand(gr.shape, device=gr.device, generator=gen)
+            sgn = torch.where(torch.rand(gr.shape, device=gr.device, generator=gen) < 0.5, -1.0, 1.0)
+            gr[u < 0.005] = 1e4
+            gr[(u >= 0.005) & (u < 0.01)] = 1e-40
+            gr.mul_(sgn.to(gr.dtype))
+
+
+def make_workload(config, device, seed=0, pdt=None):
     cfg = CONFIGS[config]
     shapes = cfg["shapes"]()
     gen = torch.Generator(device=device).manual_seed(seed)
     params, grads = [], []
     for s in shapes:
-        p = torch.empty(s, dtype=cfg["pdt"], device=device)
+        p = torch.empty(s, dtype=pdt or cfg["pdt"], device=device)
         p.normal_(0.0, 0.02, generator=gen)
         gr = torch.empty(s, dtype=cfg["gdt"], device=device)
-        gr.normal_(0.0, cfg["gscale"], generator=gen)
         p.grad_dtype = None
         p.grad = gr
         params.append(p)
         grads.append(gr)
+    fill_grads(cfg, grads, gen, seed)
     return shapes, params, grads
 
 
@@ -382,7 +431,13 @@ def run_luma(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<pass2>",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": (None if traffic_pp is None else int(traffic_pp * n_params))},
+                     "traffic": (None if traffic_pp is None else int(traffic_pp * n_params)),
+                     "traffic_source": (None if traffic_pp is None else
+                                        f"not measured in this run: ncu dram__bytes_read.sum + "
+                                        f"dram__bytes_write.sum of pass 2 per param "
+                                        f"({traffic_pp} B) from profiles/luma_pass2_{args.config}"
+                                        f".json (one Llama-3-8B layer), times this workload's "
+                                        f"params")},
         "clocks": clocks, "e2e": e2e, "gpu_launches": 2 * K,
     }
 
@@ -543,56 +598,183 @@ def result_line(args, res, world, scaling, dtype, config_out):
     return line
 
 
-def vs_reference_triton(args) -> dict:
-    """Opt-in comparison (--vs-triton, one GPU): this backend and the reference's
-    own Triton backend (installed unmodified into baseline/_ref) stepping the
-    same fp32 params and fp32 grads of the config's shapes, CUDA events over
-    the timed steps.  The reference takes fp32 params only, and its kernels
-    receive param_id as a plain int that Triton specialises to a constant for 0
-    and 1 (then `param_id.to(tl.int64)` fails to compile), so two gradless
-    tensors come first and the stepped tensors have ids >= 2."""
-    ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_dir, "luma_optimizer")):
+def reference_gpu(args, warmup: int = 2, steps: int = 3) -> dict:
+    """This backend and the reference's own GPU kernels (its Triton backend,
+    installed unmodified into baseline/_ref) stepping the same params and grads
+    of the config's shapes, one after the other on this GPU; CUDA events over
+    the timed steps.  The reference takes fp32 params only
+    (optimizer.py:443-448), so both run fp32 params with the config's grad
+    dtype.  Its kernels receive param_id as a plain int that Triton
+    specialises to a constant for 0 and 1 (then `param_id.to(tl.int64)` fails
+    to compile, at the first step of a fresh model), so two gradless tensors
+    come first and the stepped tensors have ids >= 2; the reference's code
+    path itself is unchanged."""
+    ref = reference_package()
+    if ref is None:
         return {"impl": "reference-triton", "unavailable": "reference not installed in baseline/_ref"}
-    sys.path.insert(0, ref_dir)
-    from luma_optimizer import LUMA as RefLUMA
-
     from luma_b200 import LUMA
-    shapes = CONFIGS[args.config]["shapes"]()
-    n = sum(numel(s) for s in shapes)
+    cfg = CONFIGS[args.config]
+    n = sum(numel(s) for s in cfg["shapes"]())
 
-    def make():
-        g = torch.Generator(device="cuda").manual_seed(0)
-        ps = []
-        for s in shapes:
-            p = torch.empty(s, device="cuda")
-            p.normal_(0.0, 0.02, generator=g)
-            gr = torch.empty(s, device="cuda")
-            gr.normal_(0.0, 1e-3, generator=g)
-            p.grad = gr
-            ps.append(p)
-        return ps
-
-    def timeit(opt):
-        for _ in range(max(args.warmup, 3)):
+    def timeit(make_opt):
+        torch.cuda.empty_cache()
+        _, params, _ = make_workload(args.config, torch.device("cuda"), pdt=torch.float32)
+        opt = make_opt(params)
+        for _ in range(warmup):
             opt.step()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             opt.step()
         e.record()
         torch.cuda.synchronize()
-        return s.elapsed_time(e) / args.steps
+        del opt, params
+        return s.elapsed_time(e) / steps
 
-    ours = timeit(LUMA(make(), lr=1e-3))
-    torch.cuda.empty_cache()
-    dummies = [torch.zeros(8, device="cuda") for _ in range(2)]
-    ref = timeit(RefLUMA(dummies + make(), lr=1e-3, backend="triton"))
-    return {"impl": "luma_b200 vs reference-triton", "config": args.config, "params": n,
-            "dtype": "fp32 params, fp32 grads", "steps": args.steps,
-            "luma_b200_ms": round(ours, 4), "reference_triton_ms": round(ref, 4),
-            "speedup": round(ref / ours, 2)}
+    try:
+        ours = timeit(lambda ps: LUMA(ps, lr=1e-3))
+        dummies = [torch.zeros(8, device="cuda") for _ in range(2)]
+        theirs = timeit(lambda ps: ref.LUMA(dummies + ps, lr=1e-3, backend="triton"))
+    except Exception as exc:  # noqa: BLE001
+        return {"impl": "reference-triton", "unavailable": f"{type(exc).__name__}: {str(exc)[:160]}"}
+    finally:
+        torch.cuda.empty_cache()
+    gdt = str(cfg["gdt"]).replace("torch.", "")
+    return {"impl": "reference Triton backend (baseline/_ref, unmodified) vs luma_b200, same GPU",
+            "workload": f"{args.config} shapes, fp32 params (the reference requires fp32), "
+                        f"{gdt} grads", "params": n, "warmup": warmup, "steps": steps,
+            "luma_b200_ms": round(ours, 3), "reference_triton_ms": round(theirs, 3),
+            "luma_b200_gparams": round(n / ours / 1e6, 3),
+            "reference_triton_gparams": round(n / theirs / 1e6, 3),
+            "speedup": round(theirs / ours, 2)}
+
+
+# ---------------------------------------------------------------------------
+# end-to-end training: GPT-2 small on uniform-random tokens (BASELINE config 2)
+# ---------------------------------------------------------------------------
+
+class _Block(torch.nn.Module):
+    def __init__(self, d, heads, layers):
+        super().__init__()
+        nn = torch.nn
+        self.heads = heads
+        self.ln_1, self.ln_2 = nn.LayerNorm(d), nn.LayerNorm(d)
+        self.c_attn, self.attn_proj = nn.Linear(d, 3 * d), nn.Linear(d, d)
+        self.c_fc, self.mlp_proj = nn.Linear(d, 4 * d), nn.Linear(4 * d, d)
+        for lin in (self.attn_proj, self.mlp_proj):  # GPT-2's residual-projection init
+            torch.nn.init.normal_(lin.weight, 0.0, 0.02 / math.sqrt(2 * layers))
+
+    def forward(self, x):
+        B, T, C = x.shape
+        q, k, v = self.c_attn(self.ln_1(x)).split(C, dim=2)
+        q, k, v = (t.view(B, T, self.heads, C // self.heads).transpose(1, 2) for t in (q, k, v))
+        y = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+        x = x + self.attn_proj(y.transpose(1, 2).reshape(B, T, C))
+        return x + self.mlp_proj(torch.nn.functional.gelu(self.c_fc(self.ln_2(x)),
+                                                          approximate="tanh"))
+
+
+class GPT2Small(torch.nn.Module):
+    """GPT-2 small (12 layers, d=768, 12 heads, vocab 50257, ctx 1024, lm_head
+    tied to the token embedding): 148 parameter tensors, 124,439,808 params."""
+
+    def __init__(self, vocab=50257, ctx=1024, d=768, layers=12, heads=12):
+        super().__init__()
+        nn = torch.nn
+        self.wte, self.wpe = nn.Embedding(vocab, d), nn.Embedding(ctx, d)
+        for emb in (self.wte, self.wpe):
+            torch.nn.init.normal_(emb.weight, 0.0, 0.02)
+        self.blocks = nn.ModuleList(_Block(d, heads, layers) for _ in range(layers))
+        self.ln_f = nn.LayerNorm(d)
+        self.lm_head = nn.Linear(d, vocab, bias=False)
+        self.lm_head.weight = self.wte.weight
+        for mod in self.modules():
+            if isinstance(mod, nn.Linear) and mod.bias is not None:
+                torch.nn.init.zeros_(mod.bias)
+
+    def forward(self, idx, targets):
+        pos = torch.arange(idx.shape[1], device=idx.device)
+        x = self.wte(idx) + self.wpe(pos)
+        for blk in self.blocks:
+            x = blk(x)
+        logits = self.lm_head(self.ln_f(x))
+        return torch.nn.functional.cross_entropy(logits.float().view(-1, logits.shape[-1]),
+                                                 targets.view(-1))
+
+
+def run_nanogpt(args) -> dict:
+    """LUMA (this backend) and torch's fused AdamW train GPT-2 small side by
+    side from the same init on the same uniform-random token batches (12 x
+    1024), bf16 autocast, grad-norm clipping at 1.0 before every step (the
+    reference's nanoGPT loop, benchmarks/bench_nanogpt.py:211-226; for LUMA
+    the clip is fused into the step with clip_grad_coef).  Reports training
+    throughput (tokens/s), optimizer-step time and the two loss trajectories."""
+    from luma_b200 import LUMA, clip_grad_coef
+    dev = torch.device("cuda")
+    B, T, V = 12, 1024, 50257
+    hp = dict(lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    torch.manual_seed(1337)
+    m_adamw = GPT2Small().to(dev)
+    m_luma = GPT2Small().to(dev)
+    m_luma.load_state_dict(m_adamw.state_dict())
+    n_params = sum(p.numel() for p in m_luma.parameters())
+    o_adamw = torch.optim.AdamW(m_adamw.parameters(), fused=True, **hp)
+    o_luma = LUMA(m_luma.parameters(), **hp)
+    gen = torch.Generator(device=dev).manual_seed(42)
+    stream = torch.cuda.current_stream()
+
+    def train_step(model, opt, x, y, luma):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(stream)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(x, y)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        ev[1].record(stream)
+        if luma:
+            _, coef = clip_grad_coef(model.parameters(), 1.0)
+            opt.step(grad_scale=coef)
+        else:
+            torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+            opt.step()
+        ev[2].record(stream)
+        return loss.detach(), ev
+
+    total = max(args.warmup, 3) + args.steps
+    losses = {"luma": [], "adamw": []}
+    times = {"luma": [], "adamw": []}
+    for it in range(total):
+        x = torch.randint(0, V, (B, T), device=dev, generator=gen)
+        y = torch.randint(0, V, (B, T), device=dev, generator=gen)
+        la, ea = train_step(m_adamw, o_adamw, x, y, False)
+        ll, el = train_step(m_luma, o_luma, x, y, True)
+        torch.cuda.synchronize()
+        losses["adamw"].append(float(la))
+        losses["luma"].append(float(ll))
+        if it >= total - args.steps:
+            times["adamw"].append((ea[0].elapsed_time(ea[2]), ea[1].elapsed_time(ea[2])))
+            times["luma"].append((el[0].elapsed_time(el[2]), el[1].elapsed_time(el[2])))
+    out = {}
+    for k in ("luma", "adamw"):
+        step_ms = statistics.median(t[0] for t in times[k])
+        opt_ms = statistics.median(t[1] for t in times[k])
+        out[k] = {"train_step_ms": round(step_ms, 3), "optimizer_step_ms": round(opt_ms, 4),
+                  "tokens_per_s": round(B * T / (step_ms * 1e-3), 1)}
+    gap = max(abs(a - b) / b for a, b in zip(losses["luma"], losses["adamw"]))
+    marks = sorted({0, total // 4, total // 2, total - 1})
+    return {"metric": "GPT-2 small training throughput (nanoGPT-style, uniform-random tokens, "
+                      "batch 12x1024), LUMA step on this backend",
+            "value": out["luma"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "higher_is_better": True,
+            "data": "synthetic (uniform-random token ids)", "dtype": "bf16 autocast, fp32 params",
+            "config": {"workload": "GPT-2 small (124,439,808 params, 148 tensors), batch 12x1024, "
+                                   "lr 6e-4, betas (0.9, 0.95), wd 0.1, clip 1.0",
+                       "n_params": n_params},
+            "luma": out["luma"], "adamw_fused": out["adamw"],
+            "loss": {f"step{k + 1}": {"luma": round(losses["luma"][k], 4),
+                                      "adamw": round(losses["adamw"][k], 4)} for k in marks},
+            "max_rel_loss_gap": round(gap, 5), "gpu_launches": None}
 
 
 def main():
@@ -601,7 +783,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="luma", choices=["luma", "reference"])
-    ap.add_argument("--config", default="llama8b", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="llama8b", choices=sorted(CONFIGS) + ["nanogpt"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--buckets", type=int, default=8,
@@ -612,17 +794,23 @@ def main():
                     help="N>1, copy gather: streams the peer pushes are spread over (0: one per peer)")
     ap.add_argument("--gather", default="auto", choices=["auto", "nccl", "copy"],
                     help="N>1: post-step all-gather by NCCL or by copy-engine pushes over CUDA IPC")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="one GPU: skip timing the reference's Triton backend beside this one")
     ap.add_argument("--vs-triton", action="store_true",
                     help="one GPU: also time the reference's Triton backend (baseline/_ref) on the "
                          "config's shapes in fp32 and print a comparison line")
     args = ap.parse_args()
     if args.vs_triton:
-        print(json.dumps(vs_reference_triton(args)))
+        print(json.dumps(reference_gpu(args, warmup=max(args.warmup, 2), steps=args.steps)))
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config == "nanogpt":
+        if rank == 0 and args.impl == "luma":
+            print(json.dumps(run_nanogpt(args)))
+        return
     cfg = CONFIGS[args.config]
     p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
     dtype = "f32 math; params " + str(cfg["pdt"]).replace("torch.", "") + ", grads " + \
@@ -630,12 +818,14 @@ def main():
     config_out = {"workload": cfg["name"], "bytes_per_param": p1b + p2b,
                   "l2": "inputs larger than L2 (resident params+grads+codes >> 126 MB)"
                   if args.config in ("llama8b", "ragged", "llama_layer") else "working set may fit L2",
-                  "parallelism": f"replicas{args.gpus}" if args.gpus > 1 else "single"}
+                  "parallelism": (f"zero1-dp{world} (flat shards, per-shard scales, post-step "
+                                  f"bf16 param all-gather)" if world > 1 else "single")}
 
     if args.impl == "reference":
         if rank != 0:
             return
         cb = cpu_baseline(args.config, args.steps, args.warmup, budget_s=60.0)
+        config_out["reference_params"] = "float32 (the reference rejects bf16 params)"
         line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "Gparams/s",
                 "n_gpus": args.gpus, "steps": cb["steps_timed"], "warmup": max(args.warmup, 2),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -652,11 +842,6 @@ def main():
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
                                              timeout=datetime.timedelta(seconds=300))
         res = run_zero(args, rank, world, local_rank)
-        from luma_b200.zero import auto_gather
-        mode = auto_gather(world) if args.gather == "auto" else args.gather
-        how = "copy-engine pushes over CUDA IPC" if mode == "copy" else "NCCL"
-        config_out["parallelism"] = (f"zero1-dp{world} (flat shards, per-shard scales, "
-                                     f"bf16 all-gather: {how})")
         scaling = "strong"
     else:
         if args.config == "llama70b":
@@ -668,6 +853,8 @@ def main():
         line = result_line(args, res, world, scaling, dtype, config_out)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.config, 10, 2)
+        if world == 1 and not args.no_reference_gpu:
+            line["reference_gpu"] = reference_gpu(args)
         print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LUMA_ABI_VERSION 3
+#define LUMA_ABI_VERSION 4
 
 /* Quantization grid constants (reference config.py:23-25). */
 #define LUMA_K_M 32767        /* signed int16 magnitude of Q_m        */
@@ -93,7 +93,20 @@ typedef struct LumaTensorDesc {
   uint8_t      vec_ok;       /* 1 if param/grad/q_m/q_w/u_m/u_w are 16-byte
                                 aligned (128-bit vector path)               */
   uint8_t      reserved0;
-  int64_t      reserved1;
+  void*        param_mc;     /* NULL, or the NVLink multicast (NVLS) address
+                                of `param`: pass 2 then writes the updated
+                                param through it with multimem stores, so
+                                every GPU bound to the multicast object gets
+                                it in the same step (the ZeRO all-gather fused
+                                into the step); the local copy arrives the
+                                same way.  Requires param and param_mc 8-byte
+                                aligned and, for an odd numel of bf16 params,
+                                that the 2 bytes after the last element belong
+                                to the caller (they are written: multimem
+                                stores are 32 bits wide at least).  The caller
+                                orders these writes against other readers of
+                                the peers' copies (a barrier before and after
+                                the step).                                   */
 } LumaTensorDesc;            /* 96 bytes */
 
 /*
@@ -190,6 +203,21 @@ typedef struct LumaStepArgs {
                                          218, 225), fused into both passes
                                          instead of a separate pass over the
                                          grads; the grads are not modified  */
+  float*                found_inf;    /* NULL, or a device float32 flag (the
+                                         per-device found_inf tensor of
+                                         torch.amp.GradScaler): pass 1 sets it
+                                         to 1.0 if any grad element, as stored
+                                         (before grad_scale), is inf or NaN,
+                                         the check of
+                                         torch._amp_foreach_non_finite_check_
+                                         and_unscale_; if the flag is nonzero
+                                         when pass 2 starts, the step changes
+                                         no param, code or step count (the
+                                         skipped optimizer.step() of
+                                         GradScaler.step).  Reference usage:
+                                         tests/test_mixed_precision.py:119-184,
+                                         where GradScaler.unscale_ precedes
+                                         opt.step() in a separate pass     */
 } LumaStepArgs;
 
 /*
@@ -286,6 +314,28 @@ int luma_ipc_export(const void* ptr, LumaIpcHandle* handle, uint64_t* offset);
 int luma_ipc_open(const LumaIpcHandle* handle, void** base);
 int luma_ipc_close(void* base);
 int luma_copy_async(void* dst, const void* src, uint64_t bytes, void* stream);
+
+/*
+ * Launch shape of the step kernels, for tuning reports (reference
+ * config.py:35-73 get_kernel_config): writes out[0..7] = pass-1 threads per
+ * CTA, pass-1 elements per thread per iteration, pass-1 staging stages,
+ * pass-2 threads per CTA, pass-2 elements per thread per iteration, pass-2
+ * staging stages, CTAs per SM, minimum segment length (elements) for the
+ * shared-memory decode table; returns the number written (<= n).
+ */
+int luma_launch_config(int32_t* out, int n);
+
+/*
+ * NVLink multicast copy: `bytes` bytes from `src` (this GPU's memory) to
+ * `mc_dst`, an address in a multicast (NVLS) mapping, with multimem stores
+ * on `stream` — every GPU bound to the multicast object receives the bytes at
+ * the same offset, the NVSwitch doing the fan-out (the all-gather of a ZeRO
+ * piece as one write).  Both addresses and `bytes` must be multiples of 16.
+ * Ends with a system-scope fence; the caller orders the peers' reads after it
+ * (a barrier).  No counterpart in the reference (optimizer.py:399-407 leaves
+ * gathers to FSDP).
+ */
+int luma_mc_copy(void* mc_dst, const void* src, uint64_t bytes, void* stream);
 
 /* ABI version (LUMA_ABI_VERSION). */
 int luma_abi_version(void);

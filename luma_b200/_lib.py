@@ -16,7 +16,7 @@ import numpy as np
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libluma_b200.so")
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 LUMA_OK = 0
 LUMA_ERR_INVALID = 1
@@ -30,9 +30,9 @@ F32, BF16, F16 = 0, 1, 2
 DESC_DTYPE = np.dtype({
     "names": ["param", "grad", "q_m", "q_w", "u_m", "u_w", "numel", "oct_begin", "rng_offset",
               "param_id", "row", "slot", "param_dtype", "grad_dtype", "vec_ok", "reserved0",
-              "reserved1"],
+              "param_mc"],
     "formats": ["<u8", "<u8", "<u8", "<u8", "<u8", "<u8", "<i8", "<i8", "<i8",
-                "<i4", "<i4", "<i4", "u1", "u1", "u1", "u1", "<i8"],
+                "<i4", "<i4", "<i4", "u1", "u1", "u1", "u1", "<u8"],
     "offsets": [0, 8, 16, 24, 32, 40, 48, 56, 64, 72, 76, 80, 84, 85, 86, 87, 88],
     "itemsize": 96,
 })
@@ -75,6 +75,7 @@ class LumaStepArgs(ctypes.Structure):
         ("reserved", ctypes.c_int32),
         ("step_counters", ctypes.c_void_p),
         ("grad_scale", ctypes.c_void_p),
+        ("found_inf", ctypes.c_void_p),
     ]
 
 
@@ -84,7 +85,7 @@ EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
 EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_quantize",
             "luma_abi_version", "luma_struct_sizes", "luma_last_error", "luma_arith_selfcheck",
             "luma_ipc_export", "luma_ipc_open", "luma_ipc_close", "luma_copy_async",
-            "luma_error_flags")
+            "luma_error_flags", "luma_launch_config", "luma_mc_copy")
 
 KERR_ROW_RANGE = 1  # LUMA_KERR_ROW_RANGE
 
@@ -130,6 +131,11 @@ def lib() -> ctypes.CDLL:
         h.luma_copy_async.restype = ctypes.c_int
         h.luma_copy_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                       ctypes.c_void_p]
+        h.luma_mc_copy.restype = ctypes.c_int
+        h.luma_mc_copy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
+                                   ctypes.c_void_p]
+        h.luma_launch_config.restype = ctypes.c_int
+        h.luma_launch_config.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int]
         h.luma_error_flags.restype = ctypes.c_int
         h.luma_error_flags.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]
         h.luma_step.restype = ctypes.c_int
@@ -191,6 +197,23 @@ def copy_async(dst: int, src: int, nbytes: int, stream) -> None:
     """One cudaMemcpyAsync (copy engine) of nbytes from src to dst on `stream`."""
     check(lib().luma_copy_async(ctypes.c_void_p(dst), ctypes.c_void_p(src), nbytes,
                                 ctypes.c_void_p(stream.cuda_stream)), "luma_copy_async")
+
+
+LAUNCH_KEYS = ("pass1_threads", "pass1_elems_per_thread", "pass1_stages", "pass2_threads",
+               "pass2_elems_per_thread", "pass2_stages", "ctas_per_sm", "decode_table_min_elems")
+
+
+def launch_config() -> dict[str, int]:
+    """The step kernels' launch constants as compiled into the library."""
+    out = (ctypes.c_int32 * len(LAUNCH_KEYS))()
+    k = lib().luma_launch_config(out, len(LAUNCH_KEYS))
+    return {key: int(out[i]) for i, key in enumerate(LAUNCH_KEYS[:k])}
+
+
+def mc_copy(mc_dst: int, src: int, nbytes: int, stream) -> None:
+    """Multicast (NVLS) copy of nbytes from src into a multicast mapping on `stream`."""
+    check(lib().luma_mc_copy(ctypes.c_void_p(mc_dst), ctypes.c_void_p(src), nbytes,
+                             ctypes.c_void_p(stream.cuda_stream)), "luma_mc_copy")
 
 
 def kernel_error_flags(clear: bool = False) -> int:

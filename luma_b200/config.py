@@ -1,25 +1,34 @@
 """Constants and launch configuration of the CUDA backend.
 
 The grid constants are the reference's (src/luma_optimizer/config.py:23-25).
-``get_kernel_config`` keeps the reference's function name (config.py:35-73)
-but describes this backend's launch shape: 256-thread CTAs, one octet (8
-elements, 128-bit loads) per thread per iteration, a persistent grid of
-``SMs x resident CTAs`` per pass.
+``get_kernel_config`` keeps the reference's function name and its three keys
+(config.py:35-73: ``BLOCK_SIZE``, ``num_warps``, ``num_stages``) but reports
+this backend's launch shape, read from the compiled library so it cannot
+drift from the kernels:
+
+* ``BLOCK_SIZE`` — elements one pass-2 CTA steps per loop iteration (its
+  threads x one Philox pair of 2 elements each);
+* ``num_warps`` — warps per pass-2 CTA;
+* ``num_stages`` — pass-2 shared-memory staging depth (``cp.async`` stages);
+
+plus the per-pass details (pass 1 runs 1024-thread CTAs over octets of 8
+elements, 2 staging stages), one persistent CTA per SM for both passes, and
+``sms`` when a CUDA device is given.
 """
 
 from __future__ import annotations
 
+from . import _lib
 from .hostmath import K_M, K_W, SCALE_FLOOR_M  # noqa: F401
-
-THREADS_PER_CTA = 256
-ELEMS_PER_THREAD = 8
 
 
 def get_kernel_config(device=None) -> dict[str, int]:
-    """Launch parameters of the two step kernels on ``device``."""
-    cfg = {"BLOCK_SIZE": THREADS_PER_CTA * ELEMS_PER_THREAD,
-           "threads_per_cta": THREADS_PER_CTA,
-           "elems_per_thread": ELEMS_PER_THREAD}
+    """Launch parameters of the two step kernels (and ``sms`` of ``device``)."""
+    lc = _lib.launch_config()
+    cfg = {"BLOCK_SIZE": lc["pass2_threads"] * lc["pass2_elems_per_thread"],
+           "num_warps": lc["pass2_threads"] // 32,
+           "num_stages": lc["pass2_stages"]}
+    cfg.update(lc)
     try:
         import torch
         if device is not None and torch.device(device).type == "cuda" and torch.cuda.is_available():

@@ -44,6 +44,22 @@ GetAddressRangeFn address_range_fn() {
   return fn;
 }
 
+// Grid-stride copy of 16-byte units into a multicast mapping (multimem.st of
+// four 32-bit words: the NVSwitch writes them to every bound GPU).
+__global__ void __launch_bounds__(512) luma_mc_copy_kernel(uint4* __restrict__ dst,
+                                                           const uint4* __restrict__ src,
+                                                           uint64_t n) {
+  for (uint64_t i = (uint64_t)blockIdx.x * 512 + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * 512) {
+    const uint4 v = __ldcs(src + i);
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + i),
+                 "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+                 "f"(__uint_as_float(v.w))
+                 : "memory");
+  }
+  __threadfence_system();
+}
+
 }  // namespace
 
 extern "C" {
@@ -95,6 +111,24 @@ int luma_copy_async(void* dst, const void* src, uint64_t bytes, void* stream) {
   const cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault,
                                         static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return luma_cuda_fail(e, "cudaMemcpyAsync");
+  return LUMA_OK;
+}
+
+int luma_mc_copy(void* mc_dst, const void* src, uint64_t bytes, void* stream) {
+  luma_g_err[0] = '\0';
+  if (bytes == 0) return LUMA_OK;
+  if (mc_dst == nullptr || src == nullptr)
+    return luma_fail(LUMA_ERR_INVALID, "luma_mc_copy: NULL pointer");
+  if (((uintptr_t)mc_dst | (uintptr_t)src | bytes) % 16 != 0)
+    return luma_fail(LUMA_ERR_INVALID, "luma_mc_copy: addresses and size must be multiples of 16");
+  const uint64_t n = bytes / 16;
+  const uint64_t want = (n + 511) / 512;
+  // a few CTAs suffice: the copy is bound by the NVLink links, not the SMs
+  const int blocks = (int)(want < 64 ? want : 64);
+  luma_mc_copy_kernel<<<blocks, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint4*>(mc_dst), static_cast<const uint4*>(src), n);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return luma_cuda_fail(e, "launch luma_mc_copy");
   return LUMA_OK;
 }
 

@@ -47,7 +47,7 @@ static_assert(sizeof(LumaTensorDesc) == 96, "LumaTensorDesc layout");
 static_assert(sizeof(LumaStepRow) == 56, "LumaStepRow layout");
 static_assert(sizeof(LumaGrid) == 64, "LumaGrid layout");
 static_assert(sizeof(LumaSlot) == 144, "LumaSlot layout");
-static_assert(sizeof(LumaStepArgs) == 96, "LumaStepArgs layout");
+static_assert(sizeof(LumaStepArgs) == 104, "LumaStepArgs layout");
 
 namespace {
 
@@ -218,6 +218,8 @@ struct Consts {
   // fused grad scaling (clip_grad_norm_'s coefficient), has_gscale != 0
   float gscale;
   int has_gscale;
+  // pass 1 flags non-finite grads (LumaStepArgs.found_inf != NULL)
+  int check_inf;
   // decode grid (codes as stored)
   float o_dm, o_wmin, o_dw;
   // encode grid (this step's new scales), pass 2 only
@@ -265,6 +267,17 @@ __device__ __forceinline__ void ema(const Consts& c, float g, float m, float v,
     mn = __fadd_rn(__fmul_rn(c.beta1, m), __fmul_rn(c.omb1, g));
     vn = __fadd_rn(__fmul_rn(c.beta2, v), __fmul_rn(c.omb2, g2));
   }
+}
+
+// Whether any of the n loaded grad values is inf or NaN (exponent all ones):
+// the test torch._amp_foreach_non_finite_check_and_unscale_ applies to each
+// grad element before unscaling it.
+template <int N>
+__device__ __forceinline__ int any_nonfinite(const float (&g)[N]) {
+  int bad = 0;
+#pragma unroll
+  for (int j = 0; j < N; ++j) bad |= (__float_as_uint(g[j]) & 0x7F800000u) == 0x7F800000u;
+  return bad;
 }
 
 // Fused grad scaling: g -> round_to_grad_dtype(fl32(g) * c), what
@@ -559,6 +572,7 @@ struct SegShared {
   int skip;  // capturable mode: the step's row is outside the table
   int has_gscale;  // grads are scaled by gscale (LumaStepArgs.grad_scale)
   float gscale;
+  int check_inf;   // pass 1 looks for inf / NaN grads (LumaStepArgs.found_inf)
 };
 
 // The CTA's segment state and decode table.  At namespace scope so that the
@@ -573,6 +587,7 @@ __device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Cons
   c.init = (s.row.step == 1) ? 1 : 0;
   c.gscale = s.gscale;
   c.has_gscale = s.has_gscale;
+  c.check_inf = s.check_inf;
   c.o_dm = s.dec.dm; c.o_wmin = s.dec.w_min; c.o_dw = s.dec.dw;
   if (pass2) {
     c.n_sm32 = s.enc.s_m32; c.n_dm = s.enc.dm; c.n_inv_dm = s.enc.inv_dm; c.n_inv_zm = s.enc.inv_zm;
@@ -595,6 +610,7 @@ __device__ __forceinline__ void fill_consts(const SegShared& s, bool pass2, Cons
 //          test, whose own bound never excludes it).
 struct MaxSearch {
   uint32_t am = 0u, av = 0u;
+  int bad = 0;  // a grad element seen by this thread is inf or NaN (check_inf)
   float Tm = 0.0f, Tv = 0.0f, lm = 0.0f, lv = 0.0f;
 
   // Fold the thread bounds into the warp-wide ones (all 32 lanes call this).
@@ -663,6 +679,7 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
       const int n = rem < 8 ? (int)rem : 8;
       float g[8];
       load8<GD>(d.grad, e0, n, d.vec_ok != 0 && n == 8, g);
+      if (c.check_inf) ms.bad |= any_nonfinite(g);  // padding lanes load 0
       scale_grads<GD>(c, g);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -689,6 +706,7 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
       float g[8];
       uint16_t qm[8], qw[8];
       load8<GD>(d.grad, e0, n, vec, g);
+      if (c.check_inf) ms.bad |= any_nonfinite(g);
       scale_grads<GD>(c, g);
       load8_codes(d.q_m, e0, n, vec, qm);
       load8_codes(d.q_w, e0, n, vec, qw);
@@ -749,6 +767,7 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
           g[e] = (GD == LUMA_BF16) ? __uint_as_float(h[e] << 16)
                                    : __half2float(__ushort_as_half((unsigned short)h[e]));
       }
+      if (c.check_inf) ms.bad |= any_nonfinite(g);
       scale_grads<GD>(c, g);
       const uint2 qm = *reinterpret_cast<const uint2*>(sm + o);
       const uint2 qw = *reinterpret_cast<const uint2*>(sw + o);
@@ -828,6 +847,50 @@ __device__ __forceinline__ void store2_codes(int16_t* base, int64_t e, bool both
   } else {
     p[0] = (uint16_t)q0;
     if (both) p[1] = (uint16_t)q1;
+  }
+}
+
+// Updated params through the multicast (NVLS) address of the param
+// (LumaTensorDesc.param_mc): one multimem store per pair, replicated by the
+// NVSwitch to every GPU bound to the multicast object.  Multimem stores are 32
+// bits wide at least: a bf16 pair is one 32-bit word (for a lone last element
+// the word's upper half, padding the caller owns, is written with zero); an
+// fp32 pair is one 64-bit vector store.
+__device__ __forceinline__ void mc_store_b32(void* addr, uint32_t v) {
+  asm volatile("multimem.st.relaxed.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void mc_store_f32x2(void* addr, float a, float b) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b)
+               : "memory");
+}
+
+template <int PD>
+__device__ __forceinline__ void mc_store2(void* base, int64_t e, bool both, float x0, float x1) {
+  if (PD == LUMA_F32) {
+    float* p = static_cast<float*>(base) + e;
+    if (both) {
+      mc_store_f32x2(p, x0, x1);
+    } else {
+      mc_store_b32(p, __float_as_uint(x0));
+    }
+  } else {
+    uint16_t* p = static_cast<uint16_t*>(base) + e;
+    const uint32_t h0 = __bfloat16_as_ushort(__float2bfloat16_rn(x0));
+    const uint32_t h1 = both ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(x1)) : 0u;
+    mc_store_b32(p, h0 | (h1 << 16));
+  }
+}
+
+// The updated param pair: to the multicast address when the descriptor has
+// one, else to the param itself.
+template <int PD>
+__device__ __forceinline__ void store_param2(const LumaTensorDesc& d, int64_t e, bool both,
+                                             bool vec, float x0, float x1) {
+  if (d.param_mc != nullptr) {
+    mc_store2<PD>(d.param_mc, e, both, x0, x1);
+  } else {
+    store2<PD>(d.param, e, both, vec, x0, x1);
   }
 }
 
@@ -945,7 +1008,7 @@ __device__ __forceinline__ void pass2_pairs(const LumaTensorDesc& d, const Const
     }
     pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
     pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
-    store2<PD>(d.param, e, both, vec, p0, p1);
+    store_param2<PD>(d, e, both, vec, p0, p1);
     store2_codes(d.q_m, e, both, vec, qm0, qm1);
     store2_codes(d.q_w, e, both, vec, qw0, qw1);
   }
@@ -989,7 +1052,7 @@ __device__ __forceinline__ void pass2_prefetch(const LumaTensorDesc& d, const Co
     }
     pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
     pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
-    store2<PD>(d.param, e, both, vec, p0, p1);
+    store_param2<PD>(d, e, both, vec, p0, p1);
     store2_codes(d.q_m, e, both, vec, qm0, qm1);
     store2_codes(d.q_w, e, both, vec, qw0, qw1);
     cur = nxt;
@@ -1011,7 +1074,8 @@ __device__ __forceinline__ void to_words(const typename PairWord<DT>::T& v, uint
 
 template <int PD, int GD>
 __device__ __forceinline__ void pass2_fast(const Consts& c, const float* lut, uint32_t k0,
-                                           uint32_t k1, typename PairWord<PD>::T* pp,
+                                           uint32_t k1, typename PairWord<PD>::T* mcp,
+                                           typename PairWord<PD>::T* pp,
                                            const typename PairWord<GD>::T* gp, uint32_t* qmp,
                                            uint32_t* qwp, uint64_t ctr_base, int n) {
   constexpr int kThreads = kThreadsPass2;
@@ -1039,7 +1103,9 @@ __device__ __forceinline__ void pass2_fast(const Consts& c, const float* lut, ui
     const float um1 = u24_scaled(r.z), uw1 = u24_scaled(r.w);
     pass2_elem(c, lut, g0, p0, qm0, qw0, um0, uw0);
     pass2_elem(c, lut, g1, p1, qm1, qw1, um1, uw1);
-    if constexpr (PD == LUMA_F32) {
+    if (mcp != nullptr) {
+      mc_store2<PD>(mcp, 2 * (int64_t)i, true, p0, p1);
+    } else if constexpr (PD == LUMA_F32) {
       __stcs(pp + i, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
     } else {
       __stcs(pp + i, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
@@ -1157,7 +1223,7 @@ __device__ __noinline__ void pass2_pair_exact(uint32_t k0, uint32_t k1, int64_t 
   pass2_elem(c, lut, g0, p0, qm0, qw0, u24_scaled(u.x), u24_scaled(u.y));
   pass2_elem(c, lut, g1, p1, qm1, qw1, u24_scaled(u.z), u24_scaled(u.w));
   const int64_t e = 2 * P;
-  store2<PD>(d.param, e, true, true, p0, p1);
+  store_param2<PD>(d, e, true, true, p0, p1);
   store2_codes(d.q_m, e, true, true, qm0, qm1);
   store2_codes(d.q_w, e, true, true, qw0, qw1);
 }
@@ -1170,6 +1236,7 @@ __device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, c
   using GW = typename PairWord<GD>::T;
   const LumaTensorDesc& d = s.d;
   PW* pp = static_cast<PW*>(d.param) + p_lo;
+  PW* mcp = d.param_mc != nullptr ? static_cast<PW*>(d.param_mc) + p_lo : nullptr;
   const GW* gp = static_cast<const GW*>(d.grad) + p_lo;
   uint32_t* qmp = reinterpret_cast<uint32_t*>(d.q_m) + p_lo;
   uint32_t* qwp = reinterpret_cast<uint32_t*>(d.q_w) + p_lo;
@@ -1218,7 +1285,9 @@ __device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, c
     if (rare) {
       pass2_pair_exact<PD, GD>(k0, k1, p_lo + i);
     } else {
-      if constexpr (PD == LUMA_F32) {
+      if (mcp != nullptr) {
+        mc_store2<PD>(mcp, 2 * (int64_t)i, true, p0, p1);
+      } else if constexpr (PD == LUMA_F32) {
         __stcs(pp + i, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
       } else {
         __stcs(pp + i, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
@@ -1254,7 +1323,9 @@ __device__ __forceinline__ void pass2_segment(const SegShared& s, const Consts& 
   if (steady) {
     using PW = typename PairWord<PD>::T;
     using GW = typename PairWord<GD>::T;
-    pass2_fast<PD, GD>(c, lut, k0, k1, static_cast<PW*>(d.param) + p_lo,
+    pass2_fast<PD, GD>(c, lut, k0, k1,
+                       d.param_mc != nullptr ? static_cast<PW*>(d.param_mc) + p_lo : nullptr,
+                       static_cast<PW*>(d.param) + p_lo,
                        static_cast<const GW*>(d.grad) + p_lo,
                        reinterpret_cast<uint32_t*>(d.q_m) + p_lo,
                        reinterpret_cast<uint32_t*>(d.q_w) + p_lo,
@@ -1316,6 +1387,7 @@ __device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShare
   s.skip = 0;
   s.has_gscale = a.grad_scale != nullptr;
   s.gscale = a.grad_scale != nullptr ? *a.grad_scale : 1.0f;
+  s.check_inf = a.found_inf != nullptr;
   if (a.step_counters != nullptr) {
     // Capturable mode: the step count lives on the device; the row of step t
     // is entry t - 1 of the descriptor's block of the row table.
@@ -1357,6 +1429,10 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
   const int64_t lo = (T * (int64_t)blockIdx.x) / (int64_t)gridDim.x;
   const int64_t hi = (T * ((int64_t)blockIdx.x + 1)) / (int64_t)gridDim.x;
   if (lo >= hi) return;
+  // A non-finite grad seen by pass 1 (or flagged by the caller before the
+  // step) skips the update of every tensor, as GradScaler.step skips
+  // optimizer.step().  Pass 1 has already finished: same stream.
+  if (PASS2 && a.found_inf != nullptr && *a.found_inf != 0.0f) return;
 
   if (threadIdx.x == 0) s_di = find_desc(a.descs, a.n_desc, lo);
   __syncthreads();
@@ -1410,6 +1486,9 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
           default: pass1_octets<LUMA_F16>(d, c, lut, ob, o_hi, ms); break;
         }
       }
+      if (c.check_inf) {  // (uniform) any inf / NaN grad in this CTA's part
+        if (__syncthreads_or(ms.bad) && threadIdx.x == 0) *a.found_inf = 1.0f;
+      }
       uint32_t am = ms.am, av = ms.av;
       am = __reduce_max_sync(0xffffffffu, am);
       av = __reduce_max_sync(0xffffffffu, av);
@@ -1458,6 +1537,9 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
                         ((uintptr_t)d.q_m % 4 == 0) && ((uintptr_t)d.q_w % 4 == 0) &&
                         ((uintptr_t)d.u_m % 8 == 0) && ((uintptr_t)d.u_w % 8 == 0);
       dispatch_pass2(s, lut, k0, k1, vec2, p_lo, p_hi);
+      // multicast stores become visible on the peers before anything the
+      // caller orders after the step (its cross-GPU barrier)
+      if (d.param_mc != nullptr) __threadfence_system();
     }
     __syncthreads();  // s is rewritten for the next tensor
     pos = d.oct_begin + o_hi;
@@ -1468,7 +1550,9 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
 // Capturable mode: the step count of every descriptor's slot advances by one
 // after pass 2 (each slot appears in at most one descriptor of a call).
 __global__ void __launch_bounds__(kThreads) luma_count_steps_kernel(const LumaTensorDesc* descs,
-                                                                   int n, int64_t* counters) {
+                                                                   int n, int64_t* counters,
+                                                                   const float* found_inf) {
+  if (found_inf != nullptr && *found_inf != 0.0f) return;  // skipped step
   const int i = blockIdx.x * kThreads + threadIdx.x;
   if (i < n) counters[descs[i].slot] += 1;
 }
@@ -1674,6 +1758,15 @@ int luma_error_flags(uint32_t* out, int clear) {
   return LUMA_OK;
 }
 
+int luma_launch_config(int32_t* out, int n) {
+  const int32_t v[8] = {kThreadsPass1, 8, kP1Stages, kThreadsPass2, 2, kHotStages, 1,
+                        (int32_t)kLutMinElems};
+  if (out == nullptr || n <= 0) return 0;
+  const int k = n < 8 ? n : 8;
+  for (int i = 0; i < k; ++i) out[i] = v[i];
+  return k;
+}
+
 int luma_struct_sizes(int64_t* out, int n) {
   const int64_t sizes[5] = {(int64_t)sizeof(LumaTensorDesc), (int64_t)sizeof(LumaStepRow),
                             (int64_t)sizeof(LumaGrid), (int64_t)sizeof(LumaSlot),
@@ -1718,7 +1811,7 @@ int luma_step(const LumaStepArgs* args, void* stream) {
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2");
   if (a.step_counters != nullptr) {
     luma_count_steps_kernel<<<(a.n_desc + kThreads - 1) / kThreads, kThreads, 0, s>>>(
-        a.descs, a.n_desc, a.step_counters);
+        a.descs, a.n_desc, a.step_counters, a.found_inf);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "launch step count");
   }
@@ -1861,7 +1954,7 @@ int luma_step_noalloc(const LumaStepArgs* args, void* stream) {
   if (e != cudaSuccess) return cuda_fail(e, "launch pass 2 (noalloc)");
   if (a.step_counters != nullptr) {
     luma_count_steps_kernel<<<(a.n_desc + kThreads - 1) / kThreads, kThreads, 0, s>>>(
-        a.descs, a.n_desc, a.step_counters);
+        a.descs, a.n_desc, a.step_counters, a.found_inf);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "launch step count");
   }

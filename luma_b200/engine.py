@@ -54,13 +54,14 @@ class Segment:
     rng_offset: int = 0
     u_m: torch.Tensor | None = None
     u_w: torch.Tensor | None = None
+    param_mc: int = 0  # multicast (NVLS) address of `param`, 0 for none
 
     def key(self) -> tuple:
         return (self.param.data_ptr(), self.grad.data_ptr(), self.q_m.data_ptr(),
                 self.q_w.data_ptr(), self.param.numel(), self.param_id, self.row, self.slot,
                 self.rng_offset, self.param.dtype, self.grad.dtype,
                 0 if self.u_m is None else self.u_m.data_ptr(),
-                0 if self.u_w is None else self.u_w.data_ptr())
+                0 if self.u_w is None else self.u_w.data_ptr(), self.param_mc)
 
 
 def build_desc_table(segs: list[Segment]) -> tuple[np.ndarray, int]:
@@ -87,6 +88,13 @@ def build_desc_table(segs: list[Segment]) -> tuple[np.ndarray, int]:
     d["grad_dtype"] = [dtype_code(s.grad.dtype) for s in segs]
     ptrs = np.stack([d["param"], d["grad"], d["q_m"], d["q_w"], d["u_m"], d["u_w"]])
     d["vec_ok"] = np.all(ptrs % 16 == 0, axis=0).astype(np.uint8)
+    mc = np.array([s.param_mc for s in segs], dtype=np.uint64)
+    if mc.any():
+        bad = (mc != 0) & (((mc % 8) != 0) | ((d["param"] % 8) != 0))
+        if bad.any():
+            raise ValueError("a segment with a multicast param address needs param and "
+                             "param_mc 8-byte aligned")
+    d["param_mc"] = mc
     return d, int(octs.sum())
 
 
@@ -159,12 +167,15 @@ class DeviceEngine:
     def step(self, segs: list[Segment], rows: np.ndarray | None, base_seed: int,
              stream: torch.cuda.Stream | None = None, events=None, max_ctas: int = 0,
              row_table: torch.Tensor | None = None,
-             grad_scale: torch.Tensor | None = None) -> None:
+             grad_scale: torch.Tensor | None = None,
+             found_inf: torch.Tensor | None = None) -> None:
         """Launch one step.  `rows`: this step's LumaStepRow records (uploaded);
         or, in capturable mode, `row_table`: a fixed device table (rows=None),
         with the step counts taken from and advanced in ``self.counters``.
         `grad_scale`: optional float32 device scalar every grad is multiplied
-        by (in the grad's dtype) inside the kernels."""
+        by (in the grad's dtype) inside the kernels.  `found_inf`: optional
+        float32 device flag pass 1 raises on an inf/NaN grad; when set, pass 2
+        leaves every param, code and step count unchanged."""
         if not segs:
             return
         if stream is None:
@@ -205,5 +216,6 @@ class DeviceEngine:
             a.events[i] = None if events is None else events[i]
         a.max_ctas = max_ctas
         a.grad_scale = None if grad_scale is None else grad_scale.data_ptr()
+        a.found_inf = None if found_inf is None else found_inf.data_ptr()
         _lib.check(_lib.lib().luma_step(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream)),
                    "luma_step")

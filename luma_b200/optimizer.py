@@ -177,7 +177,7 @@ class LUMA(Optimizer):
         for group in self.param_groups:
             for p in group["params"]:
                 st = self.state.get(p)
-                if not st or "_slot" not in st:
+                if not st or "_slot" not in st or "step" not in st:
                     continue
                 st["step"] = int(counts[self._unwrap_tensor(p).device][st["_slot"]])
 
@@ -199,7 +199,7 @@ class LUMA(Optimizer):
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
                 st = self.state.get(p)
-                if p.grad is None or not st or "_slot" not in st:
+                if p.grad is None or not st or "_slot" not in st or "Q_m" not in st:
                     continue
                 out["params"].append(self._unwrap_tensor(p))
                 out["grads"].append(self._unwrap_tensor(p.grad))
@@ -224,7 +224,7 @@ class LUMA(Optimizer):
         for group in self.param_groups:
             for p in group["params"]:
                 st = self.state.get(p)
-                if not st or "_slot" not in st:
+                if not st or "_slot" not in st or "step" not in st:
                     continue
                 param = self._unwrap_tensor(p)
                 g = host[param.device][st["_slot"]]["grid"][st["step"] & 1]
@@ -248,6 +248,8 @@ class LUMA(Optimizer):
         clean = {}
         for k, s in raw["state"].items():
             cs = {key: v for key, v in s.items() if not key.startswith("_")}
+            if not cs:
+                continue  # a param with a slot but no step taken yet
             p = by_index.get(k)
             if p is not None and id(p) in scales:
                 cs["S_m"], cs["S_v"] = scales[id(p)]
@@ -318,7 +320,7 @@ class LUMA(Optimizer):
             eps = group["eps"]
             for p in group["params"]:
                 st = self.state.get(p)
-                if not st:
+                if not st or "Q_m" not in st:
                     continue
                 S_m, S_v = scales[id(p)] if id(p) in scales else (st["S_m"], st["S_v"])
                 w_min, delta_m, _, delta_w, _ = precompute(S_m, S_v, eps)
@@ -418,7 +420,8 @@ class LUMA(Optimizer):
     # ------------------------------------------------------------------
     @torch.compiler.disable
     @torch.no_grad()
-    def step(self, closure=None, *, grad_scale: torch.Tensor | None = None):
+    def step(self, closure=None, *, grad_scale: torch.Tensor | None = None,
+             found_inf: torch.Tensor | None = None):
         """One optimisation step for every parameter with a gradient.
 
         ``grad_scale``: optional one-element float32 / bfloat16 / float16
@@ -432,12 +435,28 @@ class LUMA(Optimizer):
 
         Under ``torch.compile`` this method runs eagerly (one graph break at
         the call): its host side is table bookkeeping for a single library
-        call.  ``torch.ops.luma_b200.step`` is the traceable form."""
+        call.  ``torch.ops.luma_b200.step`` is the traceable form.
+
+        ``found_inf``: optional one-element float32 tensor on the params'
+        (single) device, the per-device flag of ``torch.amp.GradScaler``.  Pass
+        1 sets it to 1.0 if any grad element is inf or NaN (checked before
+        ``grad_scale`` is applied, as ``GradScaler.unscale_`` checks), and a set
+        flag makes the step change nothing, like the ``optimizer.step()`` that
+        ``GradScaler.step`` skips.  With ``grad_scale = 1/scale`` this fuses
+        ``scaler.unscale_(opt); scaler.step(opt)`` into the step's own passes
+        over the grads (``luma_b200.amp.scaler_step``).  Outside capturable
+        mode the flag is read back once after the launch (one host sync, as
+        ``GradScaler.step`` does) to keep the per-parameter ``step`` counts."""
         if grad_scale is not None:
             if not isinstance(grad_scale, torch.Tensor) or grad_scale.numel() != 1 \
                     or grad_scale.dtype not in (torch.float32, torch.bfloat16, torch.float16):
                 raise ValueError("grad_scale must be a one-element float32, bfloat16 or "
                                  "float16 tensor")
+        if found_inf is not None:
+            if not isinstance(found_inf, torch.Tensor) or found_inf.numel() != 1 \
+                    or found_inf.dtype != torch.float32 or not found_inf.is_cuda \
+                    or not found_inf.is_contiguous():
+                raise ValueError("found_inf must be a one-element contiguous float32 CUDA tensor")
         loss = None
         if closure is not None:
             with torch.enable_grad():
@@ -480,7 +499,7 @@ class LUMA(Optimizer):
         per_dev: dict[torch.device, tuple[list[Segment], dict]] = {}
         for p, param, grad, gi, pidx in work:
             state = self.state[p]
-            if len(state) == 0:
+            if "step" not in state:
                 state["step"] = 0
                 state["param_id"] = pidx
             state["step"] += 1
@@ -505,6 +524,12 @@ class LUMA(Optimizer):
                 seg.u_w = uw.reshape(-1)
             segs.append(seg)
 
+        if found_inf is not None:
+            if len(per_dev) > 1:
+                raise RuntimeError("found_inf: the fused inf check needs every stepped param on "
+                                   "one device (a skip must apply to all of them)")
+            if per_dev and found_inf.device != next(iter(per_dev)):
+                raise ValueError("found_inf must be on the params' device")
         for dev, (segs, rowmap) in per_dev.items():
             gs = None
             if grad_scale is not None:
@@ -512,7 +537,8 @@ class LUMA(Optimizer):
                 gs = self._keep_scale(dev, gs)
             if self.capturable:
                 self._engine(dev).step(segs, None, self._base_seed, events=self._step_events,
-                                       row_table=self._row_table(dev), grad_scale=gs)
+                                       row_table=self._row_table(dev), grad_scale=gs,
+                                       found_inf=found_inf)
                 continue
             rows = [None] * len(rowmap)
             for (gi, t), r in rowmap.items():
@@ -520,8 +546,21 @@ class LUMA(Optimizer):
                 rows[r] = step_row(t, g["lr"], g["betas"][0], g["betas"][1], g["eps"],
                                    g["weight_decay"])
             self._engine(dev).step(segs, rows_array(rows), self._base_seed,
-                                   events=self._step_events, grad_scale=gs)
+                                   events=self._step_events, grad_scale=gs, found_inf=found_inf)
+        if found_inf is not None and work and not self.capturable and bool(found_inf.item()):
+            self._undo_steps(work)
         return loss
+
+    def _undo_steps(self, work) -> None:
+        """A step the kernels skipped (inf/NaN grads): restore the per-param
+        step counts; a param whose first step was skipped gets no state, as if
+        ``step()`` had not been called (its slot is kept for the next try)."""
+        for p, *_ in work:
+            state = self.state[p]
+            state["step"] -= 1
+            if state["step"] == 0:
+                for key in ("step", "param_id", "Q_m", "Q_w"):
+                    state.pop(key, None)
 
     def _keep_scale(self, device: torch.device, gs: torch.Tensor) -> torch.Tensor:
         """Hold a reference to a per-device copy of the scale until the next

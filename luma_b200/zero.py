@@ -30,6 +30,17 @@ tests/test_fsdp.py:139-184), so the step partitions without any exchange:
   reads a piece about to be overwritten), the one after the last push tells
   every rank that all pieces have arrived.
 
+* ``gather="nvls"`` fuses the gather into the step itself: the flat buffer
+  lives in symmetric memory (``alloc_flat``, torch's
+  ``_symmetric_memory``) bound to an NVLink multicast object, and pass 2
+  writes every updated param through the multicast address
+  (``LumaTensorDesc.param_mc``, ``multimem.st``): the NVSwitch delivers each
+  write to every GPU, so when the step's kernels end, every replica holds
+  every rank's pieces.  No copy, no NCCL transfer, no SM taken from the step
+  beyond its own stores; a stream-ordered barrier before the step (peers are
+  done reading their replicas) and one after it (all pieces have landed)
+  bound it.
+
 Grads are read only on the owned pieces (what a reduce-scatter with the same
 layout delivers): ``grad_shard`` holds them back to back, bucket by bucket.
 """
@@ -41,7 +52,7 @@ from dataclasses import dataclass
 import torch
 
 from .engine import DeviceEngine, Segment
-from .hostmath import rows_array, step_row
+from .hostmath import grid_record, rows_array, step_row
 
 ALIGN = 8
 
@@ -72,6 +83,15 @@ class FlatLayout:
     def owned(self, rank: int, bucket: int) -> tuple[int, int]:
         lo = bucket * self.span + rank * self.piece
         return lo, lo + self.piece
+
+    def to_dict(self) -> dict:
+        return {"numels": list(self.numels), "starts": list(self.starts), "world": self.world,
+                "piece": self.piece, "buckets": self.buckets}
+
+    @staticmethod
+    def from_dict(d: dict) -> "FlatLayout":
+        return FlatLayout(tuple(int(n) for n in d["numels"]), tuple(int(s) for s in d["starts"]),
+                          int(d["world"]), int(d["piece"]), int(d["buckets"]))
 
 
 @dataclass(frozen=True)
@@ -117,6 +137,59 @@ def flat_views(flat: torch.Tensor, layout: FlatLayout, shapes) -> list[torch.Ten
     return [flat[s:s + n].view(shape) for shape, n, s in zip(shapes, layout.numels, layout.starts)]
 
 
+def alloc_flat(numel: int, dtype: torch.dtype, device, gather: str) -> torch.Tensor:
+    """The flat param buffer for ``ZeroLUMA``: symmetric memory for
+    ``gather="nvls"`` (it must be bound to a multicast object), a plain CUDA
+    tensor otherwise."""
+    if gather == "nvls":
+        import torch.distributed._symmetric_memory as symm_mem
+        return symm_mem.empty(numel, dtype=dtype, device=device)
+    return torch.empty(numel, dtype=dtype, device=device)
+
+
+class NvlsGather:
+    """Multicast (NVLS) address of a symmetric-memory flat buffer and the
+    stream-ordered barrier around the fused step.  Collective to construct;
+    raises ``PeerMapError`` on every rank if any rank cannot get a multicast
+    mapping (outcome agreed by a collective)."""
+
+    def __init__(self, flat: torch.Tensor, rank: int, process_group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        err, base = None, 0
+        try:
+            group = process_group if process_group is not None else dist.group.WORLD
+            self.handle = symm_mem.rendezvous(flat, group)
+            if not self.handle.has_multicast_support() or not self.handle.multicast_ptr:
+                err = "no NVLink multicast support on this device / driver"
+            else:
+                # the multicast mapping covers the whole symmetric buffer; the
+                # tensor sits at the same offset in it on every rank
+                local = int(self.handle.buffer_ptrs[self.handle.rank])
+                base = int(self.handle.multicast_ptr) + (flat.data_ptr() - local)
+        except Exception as exc:  # noqa: BLE001 - any failure means: no multicast
+            err = f"{type(exc).__name__}: {exc}"
+        errs = [None] * dist.get_world_size(process_group)
+        dist.all_gather_object(errs, err, group=process_group)
+        failed = [e for e in errs if e is not None]
+        if failed:
+            self.handle = None
+            raise PeerMapError(f"NVLS multicast unavailable: {failed[0]}")
+        self.mc_base = base
+        self.pg = process_group
+        self.token = torch.zeros(1, dtype=torch.float32, device=flat.device)
+
+    def barrier(self) -> None:
+        """All ranks reach this point of their streams (an all-reduce of one
+        element on the current stream)."""
+        import torch.distributed as dist
+        dist.all_reduce(self.token, group=self.pg)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.token.device)
+        self.handle = None
+
+
 def auto_gather(world: int) -> str:
     """Gather measured faster on B200 (Llama-3-8B, 8 buckets): copy engines up
     to 4 ranks (2: 196 vs 145 Gparams/s, 4: 354 vs 212), NCCL at 8 (304 vs
@@ -151,12 +224,23 @@ def gather_bucket_into(staging: torch.Tensor, shard: torch.Tensor, layout: FlatL
     return view
 
 
+class PeerMapError(RuntimeError):
+    """Some rank could not export or map the flat buffer over CUDA IPC (raised
+    on every rank, after the ranks have agreed on it)."""
+
+
 class PeerGather:
     """Copy-engine all-gather of the flat buffer's bucket pieces over CUDA IPC.
 
     Collective to construct (every rank of ``process_group``).  ``begin`` and
     ``finish`` are stream-ordered barriers on ``comm``; ``push(b, event)``
     copies this rank's piece of bucket b into every peer after ``event``.
+
+    The buffer must be plain ``cudaMalloc`` memory (PyTorch's default caching
+    allocator); memory from ``PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True``
+    is VMM-backed and has no IPC handle.  A failure to export or map on any
+    rank raises ``PeerMapError`` on all ranks (the outcome is agreed by a
+    collective, so no rank is left waiting in a later one).
     """
 
     def __init__(self, flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None,
@@ -169,17 +253,36 @@ class PeerGather:
         self.layout = layout
         self.rank = rank
         self.pg = process_group
-        handle, off = _lib.ipc_export(flat.data_ptr())
+        try:
+            info, err = _lib.ipc_export(flat.data_ptr()), None
+        except (_lib.LumaError, ValueError) as exc:
+            info, err = None, str(exc)
         infos = [None] * layout.world
-        dist.all_gather_object(infos, (handle, off), group=process_group)
+        dist.all_gather_object(infos, (info, err), group=process_group)
+        bad = [(r, e) for r, (i, e) in enumerate(infos) if i is None]
+        if bad:
+            raise PeerMapError(f"rank {bad[0][0]} cannot export its buffer over CUDA IPC: "
+                               f"{bad[0][1]}")
         self.bases = {}
         self.peer_ptr = {}
-        for p, (h, o) in enumerate(infos):
+        err = None
+        for p, (hi, _) in enumerate(infos):
             if p == rank:
                 continue
-            base = _lib.ipc_open(h)
+            try:
+                base = _lib.ipc_open(hi[0])
+            except (_lib.LumaError, ValueError) as exc:
+                err = f"rank {rank} cannot map rank {p}'s buffer: {exc}"
+                break
             self.bases[p] = base
-            self.peer_ptr[p] = base + o
+            self.peer_ptr[p] = base + hi[1]
+        errs = [None] * layout.world
+        dist.all_gather_object(errs, err, group=process_group)
+        failed = [e for e in errs if e is not None]
+        if failed:
+            for base in self.bases.values():
+                _lib.ipc_close(base)
+            raise PeerMapError(failed[0])
         dev = flat.device
         self.comm = torch.cuda.Stream(device=dev)
         order = push_order(rank, layout.world, copy_streams)
@@ -223,6 +326,19 @@ class PeerGather:
             self._lib.ipc_close(base)
         self.bases.clear()
         self.peer_ptr.clear()
+
+
+def make_peer_gather(flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None,
+                     copy_streams: int = 1) -> PeerGather | None:
+    """A PeerGather, or None (with a warning, on every rank alike) when the
+    buffer cannot be shared over CUDA IPC; the caller then gathers by NCCL."""
+    import warnings
+    try:
+        return PeerGather(flat, layout, rank, process_group, copy_streams)
+    except PeerMapError as exc:
+        warnings.warn(f"ZeroLUMA: copy-engine gather unavailable ({exc}); using NCCL instead",
+                      RuntimeWarning, stacklevel=3)
+        return None
 
 
 class ZeroLUMA:
@@ -276,8 +392,8 @@ class ZeroLUMA:
             eng.ensure_slots(max(1, len(segs)))
             self.engines.append(eng)
         self.comm = torch.cuda.Stream(device=dev)
-        if gather not in ("nccl", "copy", "auto"):
-            raise ValueError(f"gather must be 'nccl', 'copy' or 'auto', got {gather!r}")
+        if gather not in ("nccl", "copy", "auto", "nvls"):
+            raise ValueError(f"gather must be 'nccl', 'copy', 'nvls' or 'auto', got {gather!r}")
         if gather == "auto":
             gather = auto_gather(layout.world)
         self.replica = replica
@@ -288,9 +404,23 @@ class ZeroLUMA:
             if layout.world > 1:
                 self.staging = [torch.empty(layout.span, dtype=flat_param.dtype, device=dev)
                                 for _ in range(staging)]
+        self.peers = None
+        self.nvls = None
+        if gather == "nvls" and (not replica or layout.world == 1):
+            gather = "nccl" if not replica else "copy"
+        if gather == "nvls":
+            import warnings
+            try:
+                self.nvls = NvlsGather(flat_param, rank, process_group)
+            except PeerMapError as exc:
+                warnings.warn(f"ZeroLUMA: {exc}; using the copy-engine gather instead",
+                              RuntimeWarning, stacklevel=2)
+                gather = "copy"
+        if gather == "copy" and layout.world > 1:
+            self.peers = make_peer_gather(flat_param, layout, rank, process_group, copy_streams)
+            if self.peers is None:
+                gather = "nccl"
         self.gather_mode = gather
-        self.peers = PeerGather(flat_param, layout, rank, process_group, copy_streams) \
-            if gather == "copy" and layout.world > 1 else None
         self.t = 0
         self.events = None  # optional (ev0, ev1, ev2) cudaEvent_t handles for bucket 0 (timing)
 
@@ -298,15 +428,19 @@ class ZeroLUMA:
     def segments(self) -> list[ShardSegment]:
         return [sg for segs in self.bucket_segments for sg in segs]
 
-    def _engine_segments(self, b: int, grad_shard: torch.Tensor) -> list[Segment]:
+    def _engine_segments(self, b: int, grad_shard: torch.Tensor,
+                         multicast: bool = False) -> list[Segment]:
         out = []
+        es = self.flat.element_size()
         for k, sg in enumerate(self.bucket_segments[b]):
             lo = sg.local
             pos = sg.flat if self.replica else sg.local
+            mc = self.nvls.mc_base + pos * es if multicast else 0
             out.append(Segment(self.flat[pos:pos + sg.length],
                                grad_shard[lo:lo + sg.length],
                                self.q_m[lo:lo + sg.length], self.q_w[lo:lo + sg.length],
-                               param_id=sg.tensor, row=0, slot=k, rng_offset=sg.offset))
+                               param_id=sg.tensor, row=0, slot=k, rng_offset=sg.offset,
+                               param_mc=mc))
         return out
 
     def _check(self, grad_shard: torch.Tensor) -> None:
@@ -319,8 +453,8 @@ class ZeroLUMA:
                                     self.hp["weight_decay"])])
 
     def _step_bucket(self, b: int, grad_shard: torch.Tensor, rows, max_ctas: int,
-                     grad_scale: torch.Tensor | None = None) -> None:
-        segs = self._engine_segments(b, grad_shard)
+                     grad_scale: torch.Tensor | None = None, multicast: bool = False) -> None:
+        segs = self._engine_segments(b, grad_shard, multicast)
         self.engines[b].step(segs, rows, self.base_seed,
                              events=self.events if b == 0 else None, max_ctas=max_ctas,
                              grad_scale=grad_scale)
@@ -355,6 +489,16 @@ class ZeroLUMA:
         if self.layout.world == 1:
             return
         main = torch.cuda.current_stream(self.flat.device)
+        if self.nvls is not None:
+            from . import _lib
+            es = self.flat.element_size()
+            self.nvls.barrier()
+            for b in range(self.layout.buckets):
+                lo, hi = self.layout.owned(self.rank, b)
+                _lib.mc_copy(self.nvls.mc_base + lo * es, self.flat.data_ptr() + lo * es,
+                             (hi - lo) * es, main)
+            self.nvls.barrier()
+            return
         if self.peers is not None:
             self.peers.begin(main)
             done = torch.cuda.Event()
@@ -381,6 +525,13 @@ class ZeroLUMA:
                 self._step_bucket(b, grad_shard, rows, 0, grad_scale)
             return
         main = torch.cuda.current_stream(self.flat.device)
+        if self.nvls is not None:
+            # the gather is the kernels' own multicast stores
+            self.nvls.barrier()
+            for b in range(self.layout.buckets):
+                self._step_bucket(b, grad_shard, rows, 0, grad_scale, multicast=True)
+            self.nvls.barrier()
+            return
         if self.peers is not None:
             # copy engines: bucket b's pushes overlap bucket b+1's kernels
             self.peers.begin(main)
@@ -402,10 +553,65 @@ class ZeroLUMA:
         main.wait_stream(self.comm)
 
     def close(self) -> None:
-        """Unmap the peers' buffers (copy gather); call before destroying the process group."""
+        """Unmap the peers' buffers (copy gather) or drop the multicast handle
+        (nvls); call before destroying the process group."""
         if self.peers is not None:
             self.peers.close()
             self.peers = None
+        if self.nvls is not None:
+            self.nvls.close()
+            self.nvls = None
+
+    # -- checkpointing ------------------------------------------------------
+    def state_dict(self) -> dict:
+        """This rank's optimizer state (synchronises): step count, seed,
+        hyper-parameters, layout and rank, the rank's codes (``q_m``, ``q_w``,
+        ``layout.shard`` elements each, on CPU) and one ``(tensor, offset,
+        length, S_m, S_v)`` entry per local segment — the reference's
+        per-local-shard state (optimizer.py:119-144 per param: step, Q_m, Q_w,
+        S_m, S_v; one entry per shard segment here).  The params are the
+        model's state and are saved by the caller."""
+        segs = self.segments
+        scales = self.scales() if self.t > 0 else [(sg.tensor, sg.offset, 0.0, 0.0)
+                                                    for sg in segs]
+        return {"t": self.t, "base_seed": self.base_seed, "rank": self.rank,
+                "replica": self.replica, "hp": {**self.hp, "betas": tuple(self.hp["betas"])},
+                "layout": self.layout.to_dict(),
+                "q_m": self.q_m.cpu(), "q_w": self.q_w.cpu(),
+                "segments": [(sg.tensor, sg.offset, sg.length, S_m, S_v)
+                             for sg, (_, _, S_m, S_v) in zip(segs, scales)]}
+
+    def load_state_dict(self, sd: dict) -> None:
+        """Restore a ``state_dict()`` of the same rank and layout: the next
+        ``step`` continues bit for bit (same codes, grids, step count, seed)."""
+        if FlatLayout.from_dict(sd["layout"]) != self.layout:
+            raise ValueError("ZeroLUMA.load_state_dict: the checkpoint's layout differs "
+                             "(tensor sizes, world, buckets or piece)")
+        if int(sd["rank"]) != self.rank:
+            raise ValueError(f"ZeroLUMA.load_state_dict: checkpoint of rank {sd['rank']}, "
+                             f"this is rank {self.rank}")
+        segs = self.segments
+        entries = sd["segments"]
+        if len(entries) != len(segs) or any(
+                (e[0], e[1], e[2]) != (sg.tensor, sg.offset, sg.length)
+                for e, sg in zip(entries, segs)):
+            raise ValueError("ZeroLUMA.load_state_dict: segment list differs")
+        self.t = int(sd["t"])
+        self.base_seed = int(sd["base_seed"])
+        hp = dict(sd["hp"])
+        hp["betas"] = tuple(hp["betas"])
+        self.hp = hp
+        self.q_m.copy_(sd["q_m"].to(self.q_m.device, torch.int16))
+        self.q_w.copy_(sd["q_w"].to(self.q_w.device, torch.int16))
+        k = 0
+        for segs_b, eng in zip(self.bucket_segments, self.engines):
+            for j in range(len(segs_b)):
+                eng.reset_slot(j)
+                if self.t > 0:
+                    _, _, _, S_m, S_v = entries[k]
+                    eng.write_grid(j, self.t & 1, grid_record(float(S_m), float(S_v),
+                                                              self.hp["eps"]))
+                k += 1
 
     def scales(self) -> list[tuple[int, int, float, float]]:
         """(tensor, offset, S_m, S_v) of every local segment, bucket order (synchronises)."""

@@ -69,3 +69,86 @@ def uniforms(seed: int, numel: int, rng_offset: int = 0):
     u_m = (wm >> np.uint32(8)).astype(np.float32) * scale
     u_w = (ww >> np.uint32(8)).astype(np.float32) * scale
     return u_m, u_w
+
+
+# ---------------------------------------------------------------------------
+# The same stream with torch int64 tensors (CPU or CUDA), for tests that need
+# draws for hundreds of millions of elements.  A uint32 x uint32 product fits
+# in 64 bits; torch's int64 multiply keeps its low 64 bits (two's-complement
+# wrap-around), so (p >> 32) & MASK and p & MASK are the product's high and
+# low words.  Pinned against the numpy restatement above by tests/.
+# ---------------------------------------------------------------------------
+
+def _philox_torch(c0, c1, k0, k1):
+    import torch
+    mask = 0xFFFFFFFF
+    c2 = torch.zeros_like(c0)
+    c3 = torch.zeros_like(c0)
+    for _ in range(10):
+        p0 = c0 * int(M0)
+        p1 = c2 * int(M1)
+        c0, c1, c2, c3 = (((p1 >> 32) & mask) ^ c1 ^ k0, p1 & mask,
+                          ((p0 >> 32) & mask) ^ c3 ^ k1, p0 & mask)
+        k0 = (k0 + W0) & mask
+        k1 = (k1 + W1) & mask
+    return c0, c1, c2, c3
+
+
+def uniforms_torch(seed, numel: int, rng_offset: int = 0, device="cpu", chunk: int = 1 << 26):
+    """``uniforms`` as float32 torch tensors on `device`.  `seed` is one key
+    (int) or an int64 tensor of per-element keys (one tensor's key repeated,
+    for batching many tensors of one step into a single call)."""
+    import torch
+    u_m = torch.empty(numel, dtype=torch.float32, device=device)
+    u_w = torch.empty(numel, dtype=torch.float32, device=device)
+    scale = 2.0 ** -24
+    for lo in range(0, numel, chunk):
+        hi = min(numel, lo + chunk)
+        e = torch.arange(lo, hi, dtype=torch.int64, device=device) + rng_offset
+        pair = e >> 1
+        if isinstance(seed, int):
+            s = seed & 0xFFFFFFFFFFFFFFFF
+            k0, k1 = s & 0xFFFFFFFF, s >> 32
+        else:
+            s = seed[lo:hi]
+            k0, k1 = s & 0xFFFFFFFF, (s >> 32) & 0xFFFFFFFF
+        x0, x1, x2, x3 = _philox_torch(pair & 0xFFFFFFFF, pair >> 32, k0, k1)
+        odd = (e & 1).bool()
+        wm = torch.where(odd, x2, x0)
+        ww = torch.where(odd, x3, x1)
+        u_m[lo:hi] = (wm >> 8).to(torch.float32) * scale
+        u_w[lo:hi] = (ww >> 8).to(torch.float32) * scale
+    return u_m, u_w
+
+
+def step_draws_torch(base_seed: int, items, device, chunk: int = 1 << 26):
+    """Draws of one step for many tensors at once: ``items`` is a list of
+    (key, step, param_id, numel, rng_offset); returns {key: (u_m, u_w)}
+    (1-D float32 views into two shared buffers).  Elements of one chunk may
+    belong to several tensors: keys and counters are per element."""
+    import torch
+    total = sum(it[3] for it in items)
+    u_m = torch.empty(total, dtype=torch.float32, device=device)
+    u_w = torch.empty(total, dtype=torch.float32, device=device)
+    seeds = torch.empty(total, dtype=torch.int64, device=device)
+    ctr = torch.empty(total, dtype=torch.int64, device=device)
+    pos = 0
+    spans = []
+    for key, step, pid, n, off in items:
+        s = step_seed(base_seed, step, pid)
+        seeds[pos:pos + n] = s - (1 << 64) if s >= (1 << 63) else s
+        ctr[pos:pos + n] = torch.arange(off, off + n, dtype=torch.int64, device=device)
+        spans.append((key, pos, n))
+        pos += n
+    scale = 2.0 ** -24
+    for lo in range(0, total, chunk):
+        hi = min(total, lo + chunk)
+        e = ctr[lo:hi]
+        pair = e >> 1
+        s = seeds[lo:hi]
+        x0, x1, x2, x3 = _philox_torch(pair & 0xFFFFFFFF, pair >> 32, s & 0xFFFFFFFF,
+                                       (s >> 32) & 0xFFFFFFFF)
+        odd = (e & 1).bool()
+        u_m[lo:hi] = (torch.where(odd, x2, x0) >> 8).to(torch.float32) * scale
+        u_w[lo:hi] = (torch.where(odd, x3, x1) >> 8).to(torch.float32) * scale
+    return {key: (u_m[p:p + n], u_w[p:p + n]) for key, p, n in spans}

@@ -153,9 +153,26 @@ def test_new_entry_points_reject_bad_arguments_without_gpu():
     assert b"NULL" in h.luma_last_error()
 
 
-def test_step_args_carry_capturable_and_scale_fields():
+def test_step_args_carry_capturable_scale_and_found_inf_fields():
     a = _lib.LumaStepArgs()
     names = [f for f, _ in _lib.LumaStepArgs._fields_]
-    assert names[-2:] == ["step_counters", "grad_scale"]
-    assert a.step_counters is None and a.grad_scale is None
-    assert ctypes.sizeof(a) == 96
+    assert names[-3:] == ["step_counters", "grad_scale", "found_inf"]
+    assert a.step_counters is None and a.grad_scale is None and a.found_inf is None
+    assert ctypes.sizeof(a) == 104
+
+
+def test_launch_config_matches_kernel_constants():
+    from luma_b200 import get_kernel_config
+    lc = _lib.launch_config()
+    assert set(lc) == set(_lib.LAUNCH_KEYS)
+    assert lc["ctas_per_sm"] == 1 and lc["pass1_elems_per_thread"] == 8
+    assert lc["pass2_elems_per_thread"] == 2
+    assert lc["pass1_threads"] % 32 == 0 and lc["pass2_threads"] % 32 == 0
+    cfg = get_kernel_config()
+    assert cfg["BLOCK_SIZE"] == lc["pass2_threads"] * 2
+    assert cfg["num_warps"] == lc["pass2_threads"] // 32
+    assert cfg["num_stages"] == lc["pass2_stages"]
+    src = open(os.path.join(ROOT, "luma_b200", "csrc", "luma_step.cu")).read()
+    m1 = re.search(r"constexpr int kThreadsPass1 = (\d+);", src)
+    m2 = re.search(r"constexpr int kThreadsPass2 = (\d+);", src)
+    assert int(m1.group(1)) == lc["pass1_threads"] and int(m2.group(1)) == lc["pass2_threads"]

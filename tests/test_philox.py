@@ -56,3 +56,22 @@ def test_seed_mix_matches_reference_formula():
         for step, pid in ((1, 0), (2, 5), (100000, 123456)):
             ref = ((step << 32) | (pid * 2)) ^ base
             assert philox.step_seed(base, step, pid) == ref & 0xFFFFFFFFFFFFFFFF
+
+
+@pytest.mark.parametrize("seed,n,off", [(0, 17, 0), (-1234567890123, 1000, 8),
+                                        (2 ** 63 - 5, 333, 1 << 33), (-(2 ** 63), 64, 6)])
+def test_torch_stream_equals_numpy_stream(seed, n, off):
+    import torch
+    s = philox.step_seed(seed, 5, 9)
+    um, uw = philox.uniforms(s, n, off)
+    tm, tw = philox.uniforms_torch(s, n, off, chunk=100)
+    assert np.array_equal(tm.numpy(), um) and np.array_equal(tw.numpy(), uw)
+
+
+def test_batched_step_draws_equal_per_tensor_draws():
+    base = -987654321987
+    items = [("a", 3, 0, 37, 0), ("b", 3, 5, 1, 16), ("c", 3, 7, 200, 1 << 32)]
+    out = philox.step_draws_torch(base, items, "cpu", chunk=50)
+    for key, step, pid, n, off in items:
+        um, uw = philox.uniforms(philox.step_seed(base, step, pid), n, off)
+        assert np.array_equal(out[key][0].numpy(), um) and np.array_equal(out[key][1].numpy(), uw)

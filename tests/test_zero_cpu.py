@@ -191,3 +191,46 @@ def test_push_order_rotates_and_covers_peers(world, streams):
     # at every position of the order, the ranks target distinct peers (a permutation)
     for pos in range(world - 1):
         assert len({push_order(r, world, streams)[pos][0] for r in range(world)}) == world
+
+
+def _peer_fallback_worker(rank, world, port, out_q):
+    import warnings
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from luma_b200.zero import make_peer_gather
+        lay = plan_layout([100, 37], world)
+        # host memory has no CUDA IPC handle: the export fails on every rank,
+        # like VMM-backed (expandable_segments) device memory does
+        with warnings.catch_warnings(record=True) as w:
+            warnings.simplefilter("always")
+            pg = make_peer_gather(torch.zeros(lay.total), lay, rank)
+        dist.barrier()  # no rank is left inside a collective
+        out_q.put((rank, (pg is None, any("using NCCL" in str(x.message) for x in w))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_copy_gather_falls_back_to_nccl_on_every_rank_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_fallback_worker, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert all(v == (True, True) for v in results.values()), results
+
+
+def test_layout_dict_round_trip():
+    from luma_b200.zero import FlatLayout
+    lay = plan_layout([100, 37, 1, 4096], 4, 3)
+    assert FlatLayout.from_dict(lay.to_dict()) == lay
+    other = plan_layout([100, 37, 1, 4096], 2, 3)
+    assert FlatLayout.from_dict(other.to_dict()) != lay

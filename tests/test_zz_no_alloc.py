@@ -100,3 +100,50 @@ def test_noalloc_rejects_tables_beyond_its_scratch():
     status = h.luma_step_noalloc(ctypes.byref(a), None)
     assert status == _lib.LUMA_ERR_INVALID
     assert str(_lib.NOALLOC_MAX_DESCS).encode() in h.luma_last_error()
+
+
+def _compare(ref, noalloc, n, tag):
+    for i in range(n):
+        assert torch.equal(ref.params[i], noalloc.params[i]), f"{tag}: param {i} differs"
+        assert torch.equal(ref.q_m[i], noalloc.q_m[i]), f"{tag}: Q_m {i} differs"
+        assert torch.equal(ref.q_w[i], noalloc.q_w[i]), f"{tag}: Q_w {i} differs"
+    a = ref.slots.view(n, SLOT_BYTES)
+    b = noalloc.slots.view(n, SLOT_BYTES)
+    assert torch.equal(a[:, :GRID_BYTES], b[:, :GRID_BYTES]), f"{tag}: scales differ"
+
+
+def test_noalloc_accepts_exactly_its_maximum_table():
+    """LUMA_NOALLOC_MAX_DESCS tiny tensors in one call: accepted, and equal to
+    luma_step over two calls."""
+    h = _lib.lib()
+    n = _lib.NOALLOC_MAX_DESCS
+    rng = np.random.default_rng(3)
+    sizes = [int(k) for k in rng.integers(1, 100, n)]
+    gen = torch.Generator().manual_seed(4)
+    params = [(torch.randn(s, generator=gen) * 0.02).cuda() for s in sizes]
+    ref, noalloc = _CallerState(params), _CallerState(params)
+    for t in (1, 2):
+        grads = [(torch.randn(s, generator=gen) * 1e-3).cuda() for s in sizes]
+        ref.step(h.luma_step, grads, t)
+        noalloc.step(h.luma_step_noalloc, grads, t)
+        _compare(ref, noalloc, n, f"{n} tensors, call {t}")
+
+
+def test_noalloc_large_then_small_then_large_table():
+    """The scratch array is shared by every call: a large table, then a smaller
+    one, then the large one again must each match luma_step."""
+    h = _lib.lib()
+    gen = torch.Generator().manual_seed(5)
+    big_sizes = [int(s) for s in np.random.default_rng(6).integers(1, 3000, 900)] + [2_000_003]
+    small_sizes = [7, 4099, 1_000_001]
+    states = {}
+    for name, sizes in (("big", big_sizes), ("small", small_sizes)):
+        params = [(torch.randn(s, generator=gen) * 0.02).cuda() for s in sizes]
+        states[name] = (sizes, _CallerState(params), _CallerState(params))
+    for k, name in enumerate(("big", "small", "big", "small", "big")):
+        sizes, ref, noalloc = states[name]
+        t = 1 + sum(1 for x in ("big", "small", "big", "small", "big")[:k] if x == name)
+        grads = [(torch.randn(s, generator=gen) * 1e-3).cuda() for s in sizes]
+        ref.step(h.luma_step, grads, t)
+        noalloc.step(h.luma_step_noalloc, grads, t)
+        _compare(ref, noalloc, len(sizes), f"call {k} ({name} table, step {t})")
