@@ -448,7 +448,7 @@ def run_zero(args, rank, world, local_rank):
     overlapping the next bucket's kernels (strong scaling)."""
     import torch.distributed as dist
 
-    from luma_b200.zero import ZeroLUMA, plan_layout
+    from luma_b200.zero import ZeroLUMA, alloc_flat, auto_gather, plan_layout
 
     device = torch.device("cuda", local_rank)
     cfg = CONFIGS[args.config]
@@ -461,14 +461,16 @@ def run_zero(args, rank, world, local_rank):
     buckets = args.buckets if replica else max(args.buckets, 32)
     lay = plan_layout(numels, world, buckets)
     gen = torch.Generator(device=device).manual_seed(0)
-    flat = torch.empty(lay.total if replica else lay.shard, dtype=cfg["pdt"], device=device)
+    gather = auto_gather(world) if args.gather == "auto" else args.gather
+    flat = alloc_flat(lay.total if replica else lay.shard, cfg["pdt"], device,
+                      gather if replica else "nccl")
     flat.normal_(0.0, 0.02, generator=gen)
     gshard = torch.empty(lay.shard, dtype=cfg["gdt"], device=device)
     gshard.normal_(0.0, cfg["gscale"], generator=gen)
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     max_ctas = max(1, sms - args.reserve_sms) if args.reserve_sms > 0 else 0
     opt = ZeroLUMA(flat, lay, rank, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
-                   base_seed=1234, max_ctas=max_ctas, gather=args.gather,
+                   base_seed=1234, max_ctas=max_ctas, gather=gather,
                    copy_streams=args.copy_streams, replica=replica)
     for _ in range(max(args.warmup, 1)):
         opt.step(gshard)
@@ -545,6 +547,20 @@ def run_zero(args, rank, world, local_rank):
                "pipelining": "double-buffered grad shards: step k+1's upload overlaps step k"}
         del bufs, out, host
 
+    # consistency: after a full step every rank must hold the same replica
+    check = None
+    if replica:
+        opt.step(gshard)
+        torch.cuda.synchronize()
+        words = flat.view(torch.int16 if flat.element_size() == 2 else torch.int32).to(torch.int64)
+        pos = torch.arange(words.numel(), device=device, dtype=torch.int64) % 65521 + 1
+        sig = torch.stack([words.sum(), (words * pos).sum()])
+        sigs = [torch.empty_like(sig) for _ in range(world)]
+        dist.all_gather(sigs, sig)
+        check = {"replicas_equal": all(torch.equal(sigs[0], x) for x in sigs),
+                 "how": "after one more step: sum and position-weighted sum of every rank's "
+                        "replica bits, all-gathered and compared"}
+        del words, pos
     opt.close()
     p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
     peak, peak_kind = measured_peak()
@@ -559,7 +575,11 @@ def run_zero(args, rank, world, local_rank):
         "overlap_saving_ms": round(ms_local + ms_gather - ms_step, 3),
         "step_only_gparams": round(n_params / (ms_local * 1e-3) / 1e9, 3),
         "shard_params": lay.shard, "buckets": lay.buckets, "max_ctas": max_ctas,
-        "gather": opt.gather_mode, "replica": replica,
+        "gather": opt.gather_mode, "replica": replica, "check": check,
+        # fused (nvls) gather: bytes each rank receives over the whole step time,
+        # a lower bound of the rate its links sustained while the step ran
+        "gather_in_step_gbs_per_rank": (round(gather_bytes / (ms_step * 1e-3) / 1e9, 1)
+                                        if opt.gather_mode == "nvls" else None),
         "bytes_per_param": p1b + p2b, "pass2_bytes_per_param": p2b,
         "roofline": {"bound": "hbm", "kernel": "luma_pass_kernel<false>+<true> (local step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -592,7 +612,8 @@ def result_line(args, res, world, scaling, dtype, config_out):
             "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
             "gpu_launches": res["gpu_launches"]}
     for key in ("local_step_ms", "allgather_ms", "allgather_gbs_per_rank", "overlap_saving_ms",
-                "step_only_gparams", "shard_params", "buckets", "max_ctas", "gather", "replica"):
+                "step_only_gparams", "shard_params", "buckets", "max_ctas", "gather", "replica",
+                "check", "gather_in_step_gbs_per_rank"):
         if key in res:
             line[key] = res[key]
     return line
@@ -792,8 +813,9 @@ def main():
                     help="N>1, NCCL gather: SMs left free for NCCL while a gather is in flight")
     ap.add_argument("--copy-streams", type=int, default=1,
                     help="N>1, copy gather: streams the peer pushes are spread over (0: one per peer)")
-    ap.add_argument("--gather", default="auto", choices=["auto", "nccl", "copy"],
-                    help="N>1: post-step all-gather by NCCL or by copy-engine pushes over CUDA IPC")
+    ap.add_argument("--gather", default="auto", choices=["auto", "nccl", "copy", "nvls"],
+                    help="N>1: post-step all-gather by NCCL, by copy-engine pushes over CUDA IPC, "
+                         "or fused into pass 2 as NVLink multicast stores (nvls)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="one GPU: skip timing the reference's Triton backend beside this one")
     ap.add_argument("--vs-triton", action="store_true",

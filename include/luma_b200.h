@@ -92,14 +92,19 @@ typedef struct LumaTensorDesc {
   uint8_t      grad_dtype;   /* LUMA_F32 | LUMA_BF16 | LUMA_F16             */
   uint8_t      vec_ok;       /* 1 if param/grad/q_m/q_w/u_m/u_w are 16-byte
                                 aligned (128-bit vector path)               */
-  uint8_t      reserved0;
-  void*        param_mc;     /* NULL, or the NVLink multicast (NVLS) address
-                                of `param`: pass 2 then writes the updated
-                                param through it with multimem stores, so
-                                every GPU bound to the multicast object gets
-                                it in the same step (the ZeRO all-gather fused
-                                into the step); the local copy arrives the
-                                same way.  Requires param and param_mc 8-byte
+  uint8_t      mc_local;     /* with param_mc: 1 if pass 2 also stores the
+                                updated param to `param` (param_mc then maps a
+                                different buffer, e.g. the staging buffer of a
+                                sharded-params gather); 0 if param_mc maps
+                                `param` itself                              */
+  void*        param_mc;     /* NULL, or an NVLink multicast (NVLS) address:
+                                pass 2 writes the updated param through it
+                                with multimem stores, so every GPU bound to
+                                the multicast object gets it in the same step
+                                (the ZeRO all-gather fused into the step).
+                                When it maps `param` itself (mc_local = 0) the
+                                local copy arrives the same way.  Requires
+                                param and param_mc 8-byte
                                 aligned and, for an odd numel of bf16 params,
                                 that the 2 bytes after the last element belong
                                 to the caller (they are written: multimem
@@ -295,6 +300,18 @@ int luma_quantize(const float* m, const float* v, int64_t numel, const LumaGrid*
  * build) and synchronises `stream`.  No counterpart in the reference.
  */
 int luma_arith_selfcheck(uint64_t n, uint64_t seed, uint64_t* mismatches, void* stream);
+
+/*
+ * Exhaustive check of the certified logarithms used by the steady-state step
+ * loop: for every float a in [0, 2^-5] the momentum quantizer's series stays
+ * within its stated bound of CUDA's log1pf(a), and for every float z in
+ * [2^-1, 2^64] the preconditioner quantizer's approximation stays within its
+ * bound of CUDA's logf(z).  Writes the violation counts to violations[0..1]
+ * (all 0 on a correct build) and the largest errors seen to max_err[0..2]
+ * (log1p relative; log absolute where |log| < 1; log relative elsewhere);
+ * synchronises `stream`.  No counterpart in the reference.
+ */
+int luma_log_selfcheck(uint64_t* violations, double* max_err, void* stream);
 
 /*
  * Peer memory for the copy-engine all-gather of the ZeRO-1 step (one process

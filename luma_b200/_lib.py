@@ -29,7 +29,7 @@ F32, BF16, F16 = 0, 1, 2
 # so a layout drift fails the size check in lib().
 DESC_DTYPE = np.dtype({
     "names": ["param", "grad", "q_m", "q_w", "u_m", "u_w", "numel", "oct_begin", "rng_offset",
-              "param_id", "row", "slot", "param_dtype", "grad_dtype", "vec_ok", "reserved0",
+              "param_id", "row", "slot", "param_dtype", "grad_dtype", "vec_ok", "mc_local",
               "param_mc"],
     "formats": ["<u8", "<u8", "<u8", "<u8", "<u8", "<u8", "<i8", "<i8", "<i8",
                 "<i4", "<i4", "<i4", "u1", "u1", "u1", "u1", "<u8"],
@@ -85,7 +85,8 @@ EXPECTED_SIZES = (DESC_DTYPE.itemsize, ROW_DTYPE.itemsize, GRID_DTYPE.itemsize,
 EXPORTED = ("luma_step", "luma_step_noalloc", "luma_decode", "luma_quantize",
             "luma_abi_version", "luma_struct_sizes", "luma_last_error", "luma_arith_selfcheck",
             "luma_ipc_export", "luma_ipc_open", "luma_ipc_close", "luma_copy_async",
-            "luma_error_flags", "luma_launch_config", "luma_mc_copy")
+            "luma_error_flags", "luma_launch_config", "luma_mc_copy",
+            "luma_log_selfcheck")
 
 KERR_ROW_RANGE = 1  # LUMA_KERR_ROW_RANGE
 
@@ -131,6 +132,9 @@ def lib() -> ctypes.CDLL:
         h.luma_copy_async.restype = ctypes.c_int
         h.luma_copy_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                       ctypes.c_void_p]
+        h.luma_log_selfcheck.restype = ctypes.c_int
+        h.luma_log_selfcheck.argtypes = [ctypes.POINTER(ctypes.c_uint64),
+                                         ctypes.POINTER(ctypes.c_double), ctypes.c_void_p]
         h.luma_mc_copy.restype = ctypes.c_int
         h.luma_mc_copy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                    ctypes.c_void_p]
@@ -170,6 +174,17 @@ def arith_selfcheck(n: int, seed: int = 0, stream=None) -> tuple[int, int, int]:
     st = 0 if stream is None else stream.cuda_stream
     check(lib().luma_arith_selfcheck(n, seed, out, ctypes.c_void_p(st)), "luma_arith_selfcheck")
     return tuple(int(v) for v in out)
+
+
+def log_selfcheck(stream=None) -> tuple[tuple[int, int], tuple[float, float, float]]:
+    """((log1p violations, log violations), (max log1p rel err, max log abs err
+    near 1, max log rel err)) of the certified logarithms, every float of their
+    domains checked against CUDA's log1pf / logf (synchronises)."""
+    bad = (ctypes.c_uint64 * 2)()
+    err = (ctypes.c_double * 3)()
+    st = 0 if stream is None else stream.cuda_stream
+    check(lib().luma_log_selfcheck(bad, err, ctypes.c_void_p(st)), "luma_log_selfcheck")
+    return (int(bad[0]), int(bad[1])), (float(err[0]), float(err[1]), float(err[2]))
 
 
 def ipc_export(ptr: int) -> tuple[bytes, int]:

@@ -7,9 +7,10 @@ this backend's launch shape, read from the compiled library so it cannot
 drift from the kernels:
 
 * ``BLOCK_SIZE`` — elements one pass-2 CTA steps per loop iteration (its
-  threads x one Philox pair of 2 elements each);
+  threads x two Philox pairs of 2 elements each);
 * ``num_warps`` — warps per pass-2 CTA;
-* ``num_stages`` — pass-2 shared-memory staging depth (``cp.async`` stages);
+* ``num_stages`` — pass-2 shared-memory staging depth (iterations of
+  ``cp.async`` copies in flight);
 
 plus the per-pass details (pass 1 runs 1024-thread CTAs over octets of 8
 elements, 2 staging stages), one persistent CTA per SM for both passes, and

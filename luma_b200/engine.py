@@ -54,14 +54,15 @@ class Segment:
     rng_offset: int = 0
     u_m: torch.Tensor | None = None
     u_w: torch.Tensor | None = None
-    param_mc: int = 0  # multicast (NVLS) address of `param`, 0 for none
+    param_mc: int = 0  # multicast (NVLS) address the updated param goes to, 0 for none
+    mc_local: bool = False  # with param_mc: also store to `param` (param_mc maps another buffer)
 
     def key(self) -> tuple:
         return (self.param.data_ptr(), self.grad.data_ptr(), self.q_m.data_ptr(),
                 self.q_w.data_ptr(), self.param.numel(), self.param_id, self.row, self.slot,
                 self.rng_offset, self.param.dtype, self.grad.dtype,
                 0 if self.u_m is None else self.u_m.data_ptr(),
-                0 if self.u_w is None else self.u_w.data_ptr(), self.param_mc)
+                0 if self.u_w is None else self.u_w.data_ptr(), self.param_mc, self.mc_local)
 
 
 def build_desc_table(segs: list[Segment]) -> tuple[np.ndarray, int]:
@@ -95,6 +96,7 @@ def build_desc_table(segs: list[Segment]) -> tuple[np.ndarray, int]:
             raise ValueError("a segment with a multicast param address needs param and "
                              "param_mc 8-byte aligned")
     d["param_mc"] = mc
+    d["mc_local"] = [1 if (s.param_mc and s.mc_local) else 0 for s in segs]
     return d, int(octs.sum())
 
 

@@ -160,7 +160,7 @@ class NvlsGather:
         try:
             group = process_group if process_group is not None else dist.group.WORLD
             self.handle = symm_mem.rendezvous(flat, group)
-            if not self.handle.has_multicast_support() or not self.handle.multicast_ptr:
+            if not self.handle.multicast_ptr:
                 err = "no NVLink multicast support on this device / driver"
             else:
                 # the multicast mapping covers the whole symmetric buffer; the
@@ -399,16 +399,30 @@ class ZeroLUMA:
         self.replica = replica
         self.consumer = consumer
         self.staging = []
-        if not replica:
-            gather = "nccl"  # the gathered buckets go to local staging buffers
-            if layout.world > 1:
-                self.staging = [torch.empty(layout.span, dtype=flat_param.dtype, device=dev)
-                                for _ in range(staging)]
+        self.staging_mc = []
         self.peers = None
         self.nvls = None
-        if gather == "nvls" and (not replica or layout.world == 1):
-            gather = "nccl" if not replica else "copy"
-        if gather == "nvls":
+        if not replica:
+            # the gathered buckets go to rotating staging buffers: filled by the
+            # step's own multicast stores (nvls) or by NCCL
+            gather = "nvls" if gather == "nvls" and layout.world > 1 else "nccl"
+            if layout.world > 1 and gather == "nvls":
+                import warnings
+                try:
+                    self.staging = [alloc_flat(layout.span, flat_param.dtype, dev, "nvls")
+                                    for _ in range(max(staging, 2))]
+                    self.staging_mc = [NvlsGather(buf, rank, process_group)
+                                       for buf in self.staging]
+                except PeerMapError as exc:
+                    warnings.warn(f"ZeroLUMA: {exc}; gathering the buckets with NCCL instead",
+                                  RuntimeWarning, stacklevel=2)
+                    gather, self.staging, self.staging_mc = "nccl", [], []
+            if layout.world > 1 and not self.staging:
+                self.staging = [torch.empty(layout.span, dtype=flat_param.dtype, device=dev)
+                                for _ in range(staging)]
+        elif gather == "nvls" and layout.world == 1:
+            gather = "copy"
+        if gather == "nvls" and replica:
             import warnings
             try:
                 self.nvls = NvlsGather(flat_param, rank, process_group)
@@ -432,15 +446,24 @@ class ZeroLUMA:
                          multicast: bool = False) -> list[Segment]:
         out = []
         es = self.flat.element_size()
+        own_lo = self.layout.owned(self.rank, b)[0]
         for k, sg in enumerate(self.bucket_segments[b]):
             lo = sg.local
             pos = sg.flat if self.replica else sg.local
-            mc = self.nvls.mc_base + pos * es if multicast else 0
+            mc, mc_local = 0, False
+            if multicast and self.replica:
+                mc = self.nvls.mc_base + pos * es  # the replica itself
+            elif multicast:
+                # this rank's piece of the bucket's staging buffer; the shard
+                # copy is stored too
+                sm = self.staging_mc[b % len(self.staging_mc)]
+                mc = sm.mc_base + (self.rank * self.layout.piece + sg.flat - own_lo) * es
+                mc_local = True
             out.append(Segment(self.flat[pos:pos + sg.length],
                                grad_shard[lo:lo + sg.length],
                                self.q_m[lo:lo + sg.length], self.q_w[lo:lo + sg.length],
                                param_id=sg.tensor, row=0, slot=k, rng_offset=sg.offset,
-                               param_mc=mc))
+                               param_mc=mc, mc_local=mc_local))
         return out
 
     def _check(self, grad_shard: torch.Tensor) -> None:
@@ -461,6 +484,18 @@ class ZeroLUMA:
 
     def _gather_bucket(self, b: int) -> None:
         import torch.distributed as dist
+        if not self.replica and self.staging_mc:
+            # the multicast copy of this rank's piece, then every piece has landed
+            from . import _lib
+            es = self.flat.element_size()
+            sm = self.staging_mc[b % len(self.staging_mc)]
+            p = self.layout.piece
+            _lib.mc_copy(sm.mc_base + self.rank * p * es, self.flat.data_ptr() + b * p * es, p * es,
+                         torch.cuda.current_stream(self.flat.device))
+            sm.barrier()
+            if self.consumer is not None:
+                self.consumer(b, self.staging[b % len(self.staging)][:self.layout.span])
+            return
         if not self.replica:
             view = gather_bucket_into(self.staging[b % len(self.staging)], self.flat, self.layout,
                                       b, self.pg)
@@ -507,6 +542,8 @@ class ZeroLUMA:
                 self.peers.push(b, done)
             self.peers.finish(main)
             return
+        if self.staging_mc:
+            self.staging_mc[0].barrier()  # every rank is done with the last call's buckets
         for b in range(self.layout.buckets):
             self._gather_bucket(b)
 
@@ -525,6 +562,19 @@ class ZeroLUMA:
                 self._step_bucket(b, grad_shard, rows, 0, grad_scale)
             return
         main = torch.cuda.current_stream(self.flat.device)
+        if self.staging_mc:
+            # bucket b's kernels write its pieces into every rank's staging
+            # buffer b % S; the barrier after them says all pieces have landed
+            # and that every rank has run consumer(b - 1), so bucket b + 1 may
+            # overwrite the buffer bucket b - 1 used (two buffers suffice); the
+            # barrier first says every rank is done with the last call's buckets
+            self.staging_mc[0].barrier()
+            for b in range(self.layout.buckets):
+                self._step_bucket(b, grad_shard, rows, 0, grad_scale, multicast=True)
+                self.staging_mc[b % len(self.staging_mc)].barrier()
+                if self.consumer is not None:
+                    self.consumer(b, self.staging[b % len(self.staging)][:self.layout.span])
+            return
         if self.nvls is not None:
             # the gather is the kernels' own multicast stores
             self.nvls.barrier()
@@ -561,6 +611,9 @@ class ZeroLUMA:
         if self.nvls is not None:
             self.nvls.close()
             self.nvls = None
+        for sm in self.staging_mc:
+            sm.close()
+        self.staging_mc = []
 
     # -- checkpointing ------------------------------------------------------
     def state_dict(self) -> dict:

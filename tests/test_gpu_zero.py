@@ -4,7 +4,8 @@ Each rank steps its flat shard; every (tensor, shard) segment must equal the
 oracle (the reference's op sequence on CUDA) run on that segment alone with
 the backend's Philox stream (param_id = tensor index, counter offset = the
 segment's offset in the tensor).  After the all-gather (NCCL, or copy-engine
-pushes over CUDA IPC) both ranks must hold the same full parameter buffer,
+pushes over CUDA IPC, or the step's own multicast stores through NVSwitch) both
+ranks must hold the same full parameter buffer,
 and its pieces must be each owner's result.
 Skipped with fewer than 2 GPUs.
 """
@@ -33,7 +34,7 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "tests")]
-    from luma_b200.zero import ZeroLUMA, flat_views, plan_layout, shard_segments
+    from luma_b200.zero import ZeroLUMA, alloc_flat, flat_views, plan_layout, shard_segments
     from oracle import philox
     from oracle.luma_ref import OracleLUMA
 
@@ -48,11 +49,13 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
         numels = [int(torch.tensor(s).prod()) if s else 1 for s in SHAPES]
         lay = plan_layout(numels, world, buckets)
         gen = torch.Generator().manual_seed(5)
-        flat = torch.zeros(lay.total, dtype=pdt, device=dev)
+        flat = alloc_flat(lay.total, pdt, dev, gather if gather in ("nccl", "copy", "nvls")
+                          else "nccl")
+        flat.zero_()
         for v, s in zip(flat_views(flat, lay, SHAPES), SHAPES):
             v.copy_((torch.randn(s, generator=gen) * 0.02).to(pdt))
         segs = shard_segments(lay, rank)
-        sharded = gather == "sharded"
+        sharded = gather.startswith("sharded")
         if sharded:
             # params held as this rank's pieces only; buckets gathered into staging
             full = flat
@@ -62,11 +65,16 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
             def consumer(b, view):
                 gathered[b * lay.span:(b + 1) * lay.span].copy_(view)
 
+            mode = "nvls" if gather == "sharded-nvls" else "nccl"
             opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, replica=False,
-                           consumer=consumer)
+                           consumer=consumer, gather=mode)
+            if opt.gather_mode != mode:
+                msgs.append(f"{mode} unavailable: fell back to {opt.gather_mode}")
         else:
             opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, max_ctas=100,
                            gather=gather)
+            if gather == "nvls" and opt.gather_mode != "nvls":
+                msgs.append(f"nvls unavailable: fell back to {opt.gather_mode}")
 
         def pos(sg):
             return sg.local if sharded else sg.flat
@@ -124,7 +132,9 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
 
 @pytest.mark.parametrize("pdt_name,buckets,gather", [
     ("bfloat16", 1, "nccl"), ("float32", 1, "nccl"), ("bfloat16", 3, "nccl"),
-    ("bfloat16", 3, "copy"), ("float32", 1, "copy"), ("bfloat16", 3, "sharded")])
+    ("bfloat16", 3, "copy"), ("float32", 1, "copy"), ("bfloat16", 3, "sharded"),
+    ("bfloat16", 3, "nvls"), ("float32", 1, "nvls"), ("bfloat16", 3, "sharded-nvls"),
+    ("float32", 2, "sharded-nvls")])
 def test_zero_sharded_step_two_gpus(pdt_name, buckets, gather):
     world = 2
     ctx = mp.get_context("spawn")

@@ -166,10 +166,10 @@ def test_launch_config_matches_kernel_constants():
     lc = _lib.launch_config()
     assert set(lc) == set(_lib.LAUNCH_KEYS)
     assert lc["ctas_per_sm"] == 1 and lc["pass1_elems_per_thread"] == 8
-    assert lc["pass2_elems_per_thread"] == 2
+    assert lc["pass2_elems_per_thread"] == 4
     assert lc["pass1_threads"] % 32 == 0 and lc["pass2_threads"] % 32 == 0
     cfg = get_kernel_config()
-    assert cfg["BLOCK_SIZE"] == lc["pass2_threads"] * 2
+    assert cfg["BLOCK_SIZE"] == lc["pass2_threads"] * 4
     assert cfg["num_warps"] == lc["pass2_threads"] // 32
     assert cfg["num_stages"] == lc["pass2_stages"]
     src = open(os.path.join(ROOT, "luma_b200", "csrc", "luma_step.cu")).read()
