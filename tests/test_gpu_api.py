@@ -448,3 +448,151 @@ class TestLogSRUnbiasedThroughKernel:
         _, _, _, dw, _ = precompute(1e-3, S_v, eps)
         w_dec = w_min * torch.exp(q.double() * dw)
         assert abs(w_dec.mean().item() - w) / w < 1e-3
+
+
+# ---- remaining reference cases (test_convergence.py, test_state_dict.py,
+# ---- test_mixed_precision.py) ------------------------------------------------
+
+class TestReferenceCasesMore:
+    def test_mlp_regression(self):
+        """test_convergence.py:57-78: loss below 10% of its start in 300 steps."""
+        seed_all(0)
+        X = torch.randn(200, 10, device=DEV)
+        y = X @ torch.randn(10, 1, device=DEV) + 0.1 * torch.randn(200, 1, device=DEV)
+        model = nn.Sequential(nn.Linear(10, 32), nn.ReLU(), nn.Linear(32, 1)).to(DEV)
+        opt = LUMA(model.parameters(), lr=1e-3, weight_decay=0.01)
+        init = None
+        for _ in range(300):
+            opt.zero_grad()
+            loss = nn.functional.mse_loss(model(X), y)
+            init = loss.item() if init is None else init
+            loss.backward()
+            opt.step()
+        assert loss.item() < init * 0.1
+
+    def test_multi_param_groups_converge(self):
+        """test_convergence.py:80-103: two groups with their own lr."""
+        seed_all(0)
+        model = nn.Sequential(nn.Linear(10, 32), nn.ReLU(), nn.Linear(32, 1)).to(DEV)
+        opt = LUMA([{"params": model[0].parameters(), "lr": 2e-3},
+                    {"params": model[2].parameters(), "lr": 5e-4}], weight_decay=0.01)
+        X, y = torch.randn(100, 10, device=DEV), torch.randn(100, 1, device=DEV)
+        init = None
+        for _ in range(200):
+            opt.zero_grad()
+            loss = nn.functional.mse_loss(model(X), y)
+            init = loss.item() if init is None else init
+            loss.backward()
+            opt.step()
+        assert loss.item() < init * 0.5
+
+    def test_export_after_one_step_and_multi_group(self):
+        """test_state_dict.py:354-416: export at step 1; per-group hyper-
+        parameters kept, and the export loads into torch AdamW and trains."""
+        m1 = nn.Linear(8, 4).to(DEV)
+        o1 = LUMA(m1.parameters())
+        m1(torch.randn(1, 8, device=DEV)).sum().backward()
+        o1.step()
+        assert len(o1.export_adamw_state()["state"]) == 2
+        model = nn.Sequential(nn.Linear(10, 16), nn.ReLU(), nn.Linear(16, 1)).to(DEV)
+        opt = LUMA([{"params": model[0].parameters(), "lr": 2e-3},
+                    {"params": model[2].parameters(), "lr": 5e-4}], weight_decay=0.01)
+        for _ in range(3):
+            opt.zero_grad()
+            model(torch.randn(5, 10, device=DEV)).sum().backward()
+            opt.step()
+        sd = opt.export_adamw_state()
+        assert [g["lr"] for g in sd["param_groups"]] == [2e-3, 5e-4] and len(sd["state"]) == 4
+        model2 = nn.Sequential(nn.Linear(10, 16), nn.ReLU(), nn.Linear(16, 1)).to(DEV)
+        model2.load_state_dict(model.state_dict())
+        adamw = torch.optim.AdamW([{"params": model2[0].parameters(), "lr": 2e-3},
+                                   {"params": model2[2].parameters(), "lr": 5e-4}],
+                                  weight_decay=0.01)
+        adamw.load_state_dict(sd)
+        adamw.zero_grad()
+        model2(torch.randn(5, 10, device=DEV)).sum().backward()
+        adamw.step()
+        assert all(p.isfinite().all() for p in model2.parameters())
+
+    def test_import_multi_group_preserves_step_then_trains(self):
+        """test_state_dict.py:443-458, 563-608."""
+        seed_all(0)
+        model = nn.Sequential(nn.Linear(10, 16), nn.ReLU(), nn.Linear(16, 1)).to(DEV)
+        groups = lambda: [{"params": model[0].parameters(), "lr": 2e-3},  # noqa: E731
+                          {"params": model[2].parameters(), "lr": 5e-4}]
+        adamw = torch.optim.AdamW(groups(), weight_decay=0.01)
+        X = torch.randn(10, 10, device=DEV)
+        for _ in range(5):
+            adamw.zero_grad()
+            model(X).sum().backward()
+            adamw.step()
+        luma = LUMA(groups(), weight_decay=0.01)
+        luma.import_adamw_state(adamw.state_dict())
+        sd = luma.state_dict()
+        assert len(sd["state"]) == 4 and all(s["step"] == 5 for s in sd["state"].values())
+        for _ in range(5):
+            luma.zero_grad()
+            model(X).sum().backward()
+            luma.step()
+        assert all(p.isfinite().all() for p in model.parameters())
+        assert all(s["step"] == 10 for s in luma.state_dict()["state"].values())
+
+    def test_import_then_save_load_continues(self):
+        """test_state_dict.py:610-646: AdamW -> import -> train -> save -> load
+        into a fresh optimizer -> training still lowers the loss."""
+        seed_all(0)
+        loss_fn = quadratic(32)
+        kw = dict(lr=1e-2, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+        x = torch.randn(32, device=DEV, requires_grad=True)
+        adamw = torch.optim.AdamW([x], **kw)
+        train(adamw, x, loss_fn, 10)
+        luma = LUMA([x], **kw)
+        luma.import_adamw_state(adamw.state_dict())
+        train(luma, x, loss_fn, 5)
+        sd = luma.state_dict()
+        xr = x.data.clone().requires_grad_(True)
+        luma2 = LUMA([xr], **kw)
+        luma2.load_state_dict(sd)
+        before = loss_fn(xr).item()
+        train(luma2, xr, loss_fn, 10)
+        assert loss_fn(xr).item() < before
+
+    @pytest.mark.parametrize("adt", [torch.float16, torch.bfloat16])
+    def test_autocast_twenty_steps_stable_and_converges(self, adt):
+        """test_mixed_precision.py:45-117: autocast forward/backward, fp32
+        params; 20 steps finite, and the loss falls."""
+        seed_all(0)
+        model = nn.Sequential(nn.Linear(32, 64), nn.ReLU(), nn.Linear(64, 1)).to(DEV)
+        opt = LUMA(model.parameters(), lr=1e-3)
+        X, y = torch.randn(128, 32, device=DEV), torch.randn(128, 1, device=DEV)
+        losses = []
+        for _ in range(100):
+            opt.zero_grad()
+            with torch.autocast("cuda", dtype=adt):
+                loss = nn.functional.mse_loss(model(X).float(), y)
+            loss.backward()
+            opt.step()
+            losses.append(loss.item())
+            if len(losses) == 20:
+                assert all(math.isfinite(v) for v in losses)
+                assert all(p.isfinite().all() for p in model.parameters())
+        assert losses[-1] < losses[0]
+
+    def test_gradscaler_fused_converges(self):
+        """test_mixed_precision.py:119-184 with the fused unscale (amp.scaler_step)."""
+        from luma_b200.amp import scaler_step
+        seed_all(0)
+        model = nn.Sequential(nn.Linear(32, 64), nn.ReLU(), nn.Linear(64, 1)).to(DEV)
+        opt = LUMA(model.parameters(), lr=1e-3)
+        scaler = torch.amp.GradScaler("cuda")
+        X, y = torch.randn(128, 32, device=DEV), torch.randn(128, 1, device=DEV)
+        losses = []
+        for _ in range(100):
+            opt.zero_grad()
+            with torch.autocast("cuda", dtype=torch.float16):
+                loss = nn.functional.mse_loss(model(X).float(), y)
+            scaler.scale(loss).backward()
+            scaler_step(scaler, opt)
+            scaler.update()
+            losses.append(loss.item())
+        assert all(math.isfinite(v) for v in losses) and losses[-1] < losses[0]
