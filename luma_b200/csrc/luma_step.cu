@@ -67,11 +67,11 @@ constexpr size_t kLutBytes = kLutEntries * sizeof(float);
 
 // Pass-2 steady loop: each thread steps two pairs per iteration and stages
 // the raw words of its next pairs in shared memory with asynchronous copies,
-// kHotStages pair slots deep (kHotStages / 2 iterations ahead), after the
+// kHotStages pair slots deep (kHotStages / 2 - 1 iterations ahead), after the
 // decode table.  A slot holds, per thread, up to 8 bytes of param, 8 of grad,
 // 4 of Q_m and 4 of Q_w.
 #ifndef LUMA_HOT_STAGES
-#define LUMA_HOT_STAGES 6
+#define LUMA_HOT_STAGES 4
 #endif
 constexpr int kHotStages = LUMA_HOT_STAGES;
 constexpr size_t kLutPadBytes = (kLutBytes + 127) / 128 * 128;
@@ -132,14 +132,15 @@ constexpr uint32_t kPhiloxM1 = 0xCD9E8D57u;
 constexpr uint32_t kPhiloxW0 = 0x9E3779B9u;
 constexpr uint32_t kPhiloxW1 = 0xBB67AE85u;
 
+// The 32x32 -> 64-bit products are written as one 64-bit multiply each (one
+// wide multiply instruction instead of separate low and high halves).
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
-    const uint32_t lo0 = kPhiloxM0 * c.x;
-    const uint32_t hi0 = __umulhi(kPhiloxM0, c.x);
-    const uint32_t lo1 = kPhiloxM1 * c.z;
-    const uint32_t hi1 = __umulhi(kPhiloxM1, c.z);
-    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    const uint64_t p0 = (uint64_t)kPhiloxM0 * c.x;
+    const uint64_t p1 = (uint64_t)kPhiloxM1 * c.z;
+    c = make_uint4((uint32_t)(p1 >> 32) ^ c.y ^ k0, (uint32_t)p1, (uint32_t)(p0 >> 32) ^ c.w ^ k1,
+                   (uint32_t)p0);
     k0 += kPhiloxW0;
     k1 += kPhiloxW1;
   }
@@ -151,12 +152,12 @@ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1
 __device__ __forceinline__ void philox_x2(uint4& a, uint4& b, uint32_t k0, uint32_t k1) {
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
-    const uint32_t alo0 = kPhiloxM0 * a.x, ahi0 = __umulhi(kPhiloxM0, a.x);
-    const uint32_t alo1 = kPhiloxM1 * a.z, ahi1 = __umulhi(kPhiloxM1, a.z);
-    const uint32_t blo0 = kPhiloxM0 * b.x, bhi0 = __umulhi(kPhiloxM0, b.x);
-    const uint32_t blo1 = kPhiloxM1 * b.z, bhi1 = __umulhi(kPhiloxM1, b.z);
-    a = make_uint4(ahi1 ^ a.y ^ k0, alo1, ahi0 ^ a.w ^ k1, alo0);
-    b = make_uint4(bhi1 ^ b.y ^ k0, blo1, bhi0 ^ b.w ^ k1, blo0);
+    const uint64_t pa0 = (uint64_t)kPhiloxM0 * a.x, pa1 = (uint64_t)kPhiloxM1 * a.z;
+    const uint64_t pb0 = (uint64_t)kPhiloxM0 * b.x, pb1 = (uint64_t)kPhiloxM1 * b.z;
+    a = make_uint4((uint32_t)(pa1 >> 32) ^ a.y ^ k0, (uint32_t)pa1,
+                   (uint32_t)(pa0 >> 32) ^ a.w ^ k1, (uint32_t)pa0);
+    b = make_uint4((uint32_t)(pb1 >> 32) ^ b.y ^ k0, (uint32_t)pb1,
+                   (uint32_t)(pb0 >> 32) ^ b.w ^ k1, (uint32_t)pb0);
     k0 += kPhiloxW0;
     k1 += kPhiloxW1;
   }
@@ -736,6 +737,42 @@ __device__ __forceinline__ void pass1_elem(const Consts& c, const float* lut, co
   }
 }
 
+// pass1_elem for the four elements of a quad when both tables are present:
+// the four bounds are tested first and one branch per quad takes the exact
+// decode of the elements that need it (a skip is justified against the
+// maxima at the start of the quad, which only grow).
+__device__ __forceinline__ void pass1_quad_tables(const Consts& c, const float* lut,
+                                                  const float* vbt, const float (&g)[4],
+                                                  const uint32_t (&qmw)[2], const uint32_t (&qww)[2],
+                                                  MaxSearch& ms) {
+  float g2[4];
+  bool need[4];
+  bool any = false;
+  const float amax = __uint_as_float(ms.av);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int q = (int)(int16_t)(uint16_t)(qmw[e >> 1] >> (16 * (e & 1)));
+    const float mne = __fadd_rn(__fmul_rn(c.beta1, decode_m_lut(q, lut)), __fmul_rn(c.omb1, g[e]));
+    ms.am = max(ms.am, __float_as_uint(fabsf(mne)));
+    const uint32_t qw = (qww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+    g2[e] = __fmul_rn(c.omb2, __fmul_rn(g[e], g[e]));
+    const float ub = __fadd_rn(__fmul_rn(c.beta2, vbt[qw >> 8]), g2[e]);
+    need[e] = !(ub <= amax) && !(ub <= ms.Tv);
+    any |= need[e];
+  }
+  if (any) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (need[e]) {
+        const uint32_t qw = (qww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+        const float vne = __fadd_rn(__fmul_rn(c.beta2, decode_v(qw, c.o_wmin, c.o_dw, c.eps32)), g2[e]);
+        ms.av = max(ms.av, __float_as_uint(vne));
+        ms.lv = fmaxf(ms.lv, vne);
+      }
+    }
+  }
+}
+
 // Pass 1 over octets [o_lo, o_hi): one octet per thread per iteration, loaded
 // straight into registers (16-byte loads when aligned).  Staging tiles through
 // shared memory with bulk copies measured slower on B200 (the block barriers
@@ -847,11 +884,15 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
       const uint2 qm = *reinterpret_cast<const uint2*>(sm + o);
       const uint2 qw = *reinterpret_cast<const uint2*>(sw + o);
       const uint32_t qmw[2] = {qm.x, qm.y}, qww[2] = {qw.x, qw.y};
+      if (vbt != nullptr) {
+        pass1_quad_tables(c, lut, vbt, g, qmw, qww, ms);
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t wm = qmw[e >> 1] >> (16 * (e & 1));
-        const uint32_t ww = (qww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
-        pass1_elem(c, lut, vbt, g[e], (int)(int16_t)(uint16_t)wm, ww, ms);
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t wm = qmw[e >> 1] >> (16 * (e & 1));
+          const uint32_t ww = (qww[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+          pass1_elem(c, lut, vbt, g[e], (int)(int16_t)(uint16_t)wm, ww, ms);
+        }
       }
     }
     st = st == kP1Stages - 1 ? 0 : st + 1;
@@ -1304,9 +1345,11 @@ __device__ __noinline__ void pass2_pair_exact(uint32_t k0, uint32_t k1, int64_t 
 // The steady loop over n complete pairs starting at pair p_lo of the segment.
 // Each thread takes pairs i and i + kThreads of every block of 2 * kThreads
 // (both coalesced across the warp): one interleaved Philox evaluation for the
-// two, two independent element chains each, and kHotStages / 2 iterations of
-// copies in flight.  Measured on one Llama-3-8B layer (bf16): 512 threads x 2
-// pairs 1.81 ms, 640 x 1 pair 1.89 ms, 640 x 2 pairs 1.96 ms (register spills).
+// two, two independent element chains each, and the copies of the next
+// kHotStages / 2 - 1 iterations in flight.  Measured on one Llama-3-8B layer
+// (bf16): 512 threads x 2 pairs 1.80 ms with copies 1 iteration ahead, 1.82 ms
+// 2 iterations ahead; 640 x 1 pair 1.89 ms, 640 x 2 pairs 1.96 ms (register
+// spills), 448 x 2 pairs 2.07 ms.
 template <int PD, int GD>
 __device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, const float* lut,
                                            uint32_t k0, uint32_t k1, int64_t p_lo, int n) {
@@ -1553,21 +1596,25 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
     fill_consts(s, PASS2, c);
     // Decode table for long segments of quantized (t >= 2) tensors; in pass
     // 1 also the bucket maxima of v(q) (256 buckets of 256 codes): thread i
-    // evaluates codes [64 i, 64 i + 64), four consecutive lanes one bucket.
+    // evaluates codes [c i, c i + c) with c = 65536 / threads, and the
+    // 256 / c consecutive lanes of a bucket combine their maxima.
     const float* lut = nullptr;
     const float* vbt = nullptr;
     if (lut_ok && !c.init && (o_hi - o_lo) * 8 >= kLutMinElems) {
       for (int i = threadIdx.x; i < kLutEntries; i += kThreads)
         s_lut[i] = expm1f(__fmul_rn((float)i, c.o_dm));
       if (!PASS2) {
-        static_assert(PASS2 || kThreads * 64 == 65536, "one thread per 64 codes");
+        constexpr int kCodes = 65536 / kThreads;     // codes per thread
+        constexpr int kLanes = 256 / kCodes;         // lanes per bucket
+        static_assert(PASS2 || (kCodes * kThreads == 65536 && kLanes >= 1 && kLanes <= 32),
+                      "bucket table layout");
         uint32_t mx = 0u;
-        for (int j = 0; j < 64; ++j)
-          mx = max(mx, __float_as_uint(decode_v((uint32_t)(threadIdx.x * 64 + j), c.o_wmin, c.o_dw,
-                                                c.eps32)));
-        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        if ((threadIdx.x & 3) == 0) s_vbound[threadIdx.x >> 2] = __uint_as_float(mx);
+        for (int j = 0; j < kCodes; ++j)
+          mx = max(mx, __float_as_uint(decode_v((uint32_t)(threadIdx.x * kCodes + j), c.o_wmin,
+                                                c.o_dw, c.eps32)));
+#pragma unroll
+        for (int k = 1; k < kLanes; k <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, k));
+        if (threadIdx.x % kLanes == 0) s_vbound[threadIdx.x / kLanes] = __uint_as_float(mx);
         vbt = s_vbound;
       }
       __syncthreads();

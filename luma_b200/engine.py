@@ -43,7 +43,8 @@ def dtype_code(dt: torch.dtype) -> int:
 
 @dataclass
 class Segment:
-    """One descriptor: a whole tensor or one shard segment of it (1-D views)."""
+    """One descriptor: a whole tensor or one shard segment of it.  The four
+    tensors are contiguous and of equal numel; their shapes do not matter."""
     param: torch.Tensor
     grad: torch.Tensor
     q_m: torch.Tensor

@@ -30,6 +30,7 @@ from .hostmath import SCALE_FLOOR_M, grid_record, precompute, rows_array, step_r
 _BACKENDS = {"auto", "cuda", "triton"}
 _PARAM_DTYPES = (torch.float32, torch.bfloat16)
 _GRAD_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
+_PLAIN_TENSOR_TYPES = (torch.Tensor, torch.nn.Parameter)
 
 
 class LUMA(Optimizer):
@@ -462,16 +463,22 @@ class LUMA(Optimizer):
             with torch.enable_grad():
                 loss = closure()
 
-        # Pass A: validate everything before touching any state.
+        # Pass A: validate everything before touching any state.  This loop
+        # and the next run once per tensor every step, so they avoid per-tensor
+        # torch calls that allocate (views, device objects): with 10,000
+        # tensors every microsecond per tensor is 10 ms per step.
         work = []
         param_idx = 0
+        plain = _PLAIN_TENSOR_TYPES
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
                 param_idx += 1
-                if p.grad is None:
+                grad = p.grad
+                if grad is None:
                     continue
-                param = self._unwrap_tensor(p)
-                grad = self._unwrap_tensor(p.grad)
+                param = p if type(p) in plain else self._unwrap_tensor(p)
+                if type(grad) not in plain:
+                    grad = self._unwrap_tensor(grad)
                 if param.numel() == 0:
                     continue  # empty FSDP shard on this rank
                 if grad.is_sparse:
@@ -485,7 +492,8 @@ class LUMA(Optimizer):
                 if not param.is_cuda:
                     raise RuntimeError(
                         f"LUMA backend 'cuda' requires CUDA tensors (param on {param.device}).")
-                if grad.device != param.device:
+                dev = param.get_device()
+                if grad.get_device() != dev:
                     raise ValueError("LUMA requires the gradient on the parameter's device")
                 if grad.shape != param.shape:
                     raise ValueError("LUMA requires the gradient to have the parameter's shape")
@@ -493,11 +501,11 @@ class LUMA(Optimizer):
                     raise ValueError("LUMA CUDA kernel requires contiguous parameters")
                 if not grad.is_contiguous():
                     raise ValueError("LUMA CUDA kernel requires contiguous gradients")
-                work.append((p, param, grad, gi, param_idx - 1))
+                work.append((p, param, grad, gi, param_idx - 1, dev))
 
         # Pass B: state bookkeeping and per-device segment lists.
-        per_dev: dict[torch.device, tuple[list[Segment], dict]] = {}
-        for p, param, grad, gi, pidx in work:
+        per_idx: dict[int, tuple[list[Segment], dict]] = {}
+        for p, param, grad, gi, pidx, dev in work:
             state = self.state[p]
             if "step" not in state:
                 state["step"] = 0
@@ -509,13 +517,13 @@ class LUMA(Optimizer):
                 state["Q_w"] = torch.empty_like(param, dtype=torch.int16)
             if "_slot" not in state:
                 state["_slot"] = self._new_slot(param.device)
-            segs, rowmap = per_dev.setdefault(param.device, ([], {}))
+            segs, rowmap = per_idx.setdefault(dev, ([], {}))
             if self.capturable:
                 row = gi * self.capture_steps  # the group's block of the row table
             else:
                 row = rowmap.setdefault((gi, t), len(rowmap))
-            seg = Segment(param.view(-1), grad.view(-1), state["Q_m"].view(-1),
-                          state["Q_w"].view(-1), state["param_id"], row, state["_slot"])
+            seg = Segment(param, grad, state["Q_m"], state["Q_w"], state["param_id"], row,
+                          state["_slot"])
             if self._draw_hook is not None:
                 if self.capturable:
                     raise RuntimeError("the draw hook is not available in capturable mode")
@@ -524,6 +532,7 @@ class LUMA(Optimizer):
                 seg.u_w = uw.reshape(-1)
             segs.append(seg)
 
+        per_dev = {torch.device("cuda", k): v for k, v in per_idx.items()}
         if found_inf is not None:
             if len(per_dev) > 1:
                 raise RuntimeError("found_inf: the fused inf check needs every stepped param on "

@@ -60,7 +60,7 @@ def step(params: list[torch.Tensor], grads: list[torch.Tensor], q_m: list[torch.
     `grad_scale` (optional float32 scalar) is fused as in ``LUMA.step``."""
     if not params:
         return
-    segs = [Segment(p.view(-1), g.view(-1), m.view(-1), w.view(-1), pid, rb, sl)
+    segs = [Segment(p, g, m, w, pid, rb, sl)
             for p, g, m, w, pid, sl, rb in zip(params, grads, q_m, q_w, param_ids, slot_ids,
                                                row_bases)]
     descs, total = _desc_table(segs, params[0].device)
