@@ -1,7 +1,8 @@
 """Benchmark of the LUMA optimizer step on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl luma|reference]
-                    [--config llama8b|gpt2|ragged|cpu21m]
+                    [--config llama8b|llama70b|llama_layer|gpt2|ragged|cpu21m|nanogpt]
+                    [--gather auto|nvls|copy|nccl]
 
 A "step" is one ``LUMA.step()`` over every parameter tensor of the workload
 (two kernel launches).  Default workload: Llama-3-8B parameter shapes (291
