@@ -176,3 +176,14 @@ def test_launch_config_matches_kernel_constants():
     m1 = re.search(r"constexpr int kThreadsPass1 = (\d+);", src)
     m2 = re.search(r"constexpr int kThreadsPass2 = (\d+);", src)
     assert int(m1.group(1)) == lc["pass1_threads"] and int(m2.group(1)) == lc["pass2_threads"]
+
+
+def test_plain_c_consumer_builds_against_the_header(tmp_path):
+    """``tests/c_abi/step_from_c.c`` (the C host the GPU test runs) compiles as
+    warning-free C11 against ``include/luma_b200.h`` and links the library."""
+    lib = os.path.join(ROOT, "luma_b200", "_lib")
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    "-I", os.path.join(cuda, "include"), os.path.join(ROOT, "tests", "c_abi", "step_from_c.c"),
+                    "-o", str(tmp_path / "step_from_c"), "-L", lib, "-lluma_b200",
+                    "-L", os.path.join(cuda, "lib64"), "-lcudart", "-lm", f"-Wl,-rpath,{lib}"], check=True)
