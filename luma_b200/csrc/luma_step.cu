@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cfloat>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -672,12 +673,89 @@ struct MaxSearch {
   int bad = 0;  // a grad element seen by this thread is inf or NaN (check_inf)
   float Tm = 0.0f, Tv = 0.0f, lm = 0.0f, lv = 0.0f;
 
-  // Fold the thread bounds into the warp-wide ones (all 32 lanes call this).
+  // Fold the thread bounds, and the exact maxima (values of actual elements,
+  // so lower bounds of the tensor's maxima), into the warp-wide ones (all 32
+  // lanes call this).  fmaxf drops a NaN maximum; the clamp at 0 keeps the
+  // reduced bit patterns those of non-negative floats.
   __device__ __forceinline__ void warp_sync_bounds() {
-    Tm = fmaxf(Tm, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lm))));
-    Tv = fmaxf(Tv, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(lv))));
+    const float xm = fmaxf(fmaxf(lm, __uint_as_float(am)), 0.0f);
+    const float xv = fmaxf(fmaxf(lv, __uint_as_float(av)), 0.0f);
+    Tm = fmaxf(Tm, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(xm))));
+    Tv = fmaxf(Tv, __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(xv))));
   }
 };
+
+// Packed 16-bit minima / maxima (two lanes per 32-bit word).
+__device__ __forceinline__ uint32_t vmax_s16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t vmin_s16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t vmax_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t vmin_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// G = max |g| over the four staged grads of a quad, from their bit patterns:
+// the largest magnitude pattern, so an inf or NaN grad makes G inf or NaN
+// (NaN patterns order above inf).  `bad`: one of them is inf or NaN.
+template <int GD>
+__device__ __forceinline__ float quad_gmax(const unsigned char* s, int& bad) {
+  if constexpr (GD == LUMA_F32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(s);
+    const uint32_t b = max(max(v.x & 0x7FFFFFFFu, v.y & 0x7FFFFFFFu),
+                           max(v.z & 0x7FFFFFFFu, v.w & 0x7FFFFFFFu));
+    bad = b >= 0x7F800000u;
+    return __uint_as_float(b);
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(s);
+    const uint32_t h = vmax_u16x2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu);
+    const uint32_t b = max(h & 0xFFFFu, h >> 16);
+    if constexpr (GD == LUMA_BF16) {
+      bad = b >= 0x7F80u;
+      return __uint_as_float(b << 16);
+    } else {
+      bad = b >= 0x7C00u;
+      return __half2float(__ushort_as_half((unsigned short)b));
+    }
+  }
+}
+
+// Whether a quad may hold the tensor's largest |m'| or v' above the running
+// thresholds (pass 1, both tables present, decode table non-decreasing,
+// bucket table non-increasing).  With G = max |g| (after the grad scaling),
+// M = lut[max |q_m|] >= |m| and V = vbt[min q_w >> 8] >= v for all four
+// elements, every rounded operation below is monotone in its operands, so
+//   |m'| = |fl(fl(b1 m) + fl(c1 g))| <= fl(fl(b1 M) + fl(c1 G)) = ubm,
+//   v'   =  fl(fl(b2 v) + fl(c2 fl(g g))) <= fl(fl(b2 V) + fl(c2 fl(G G))) = ubv.
+// A quad with ubm <= thr_m and ubv <= thr_v (finite thresholds, each the value
+// of an element already seen) cannot raise either maximum and is skipped.  A
+// non-finite bound (inf / NaN grad or table entry) never compares <= a finite
+// threshold, so such quads are always evaluated exactly.
+__device__ __forceinline__ bool quad_may_raise(const Consts& c, const float* lut, const float* vbt,
+                                               float G, uint2 qm, uint2 qw, float thr_m,
+                                               float thr_v) {
+  const uint32_t hi = vmax_s16x2(qm.x, qm.y), lo = vmin_s16x2(qm.x, qm.y);
+  const int mx = max((int)(int16_t)(uint16_t)hi, (int)hi >> 16);
+  const int mn = min((int)(int16_t)(uint16_t)lo, (int)lo >> 16);
+  const float M = lut[max(mx, -mn)];
+  const uint32_t w = vmin_u16x2(qw.x, qw.y);
+  const float V = vbt[min(w & 0xFFFFu, w >> 16) >> 8];
+  const float ubm = __fadd_rn(__fmul_rn(c.beta1, M), __fmul_rn(c.omb1, G));
+  const float ubv = __fadd_rn(__fmul_rn(c.beta2, V), __fmul_rn(c.omb2, __fmul_rn(G, G)));
+  return !(ubm <= thr_m) || !(ubv <= thr_v);
+}
 
 // One element of pass 1 (step >= 2): exact |m'| from the decode table when
 // there is one, certified-bound candidates otherwise.  v': with the bucket
@@ -837,8 +915,8 @@ __device__ __forceinline__ void pass1_octets(const LumaTensorDesc& d, const Cons
 // registers.  All threads run the same number of iterations (warp reductions).
 template <int GD>
 __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Consts& c,
-                                             const float* lut, const float* vbt, int64_t q_lo,
-                                             int64_t q_hi, MaxSearch& ms) {
+                                             const float* lut, const float* vbt, bool qb,
+                                             int64_t q_lo, int64_t q_hi, MaxSearch& ms) {
   constexpr int kThreads = kThreadsPass1;
   constexpr int kGB = GD == LUMA_F32 ? 16 : 8;  // grad bytes per quad
   unsigned char* stage0 = reinterpret_cast<unsigned char*>(g_lut) + kLutPadBytes;
@@ -865,8 +943,20 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
     const int64_t j = jb + threadIdx.x;
     issue(j + (int64_t)(kP1Stages - 1) * kThreads, st == 0 ? kP1Stages - 1 : st - 1);
     cp_async_wait<kP1Stages - 1>();  // quad j has landed
-    if (j < n) {
-      const size_t o = (size_t)st * kP1StageBytes;
+    // finite thresholds: the largest exact maxima known to this lane
+    const float thr_m = fminf(fmaxf(__uint_as_float(ms.am), ms.Tm), FLT_MAX);
+    const float thr_v = fminf(fmaxf(__uint_as_float(ms.av), ms.Tv), FLT_MAX);
+    const size_t o = (size_t)st * kP1StageBytes;
+    bool exact = j < n;
+    if (qb && exact) {  // one bound per quad; see quad_may_raise
+      int bad;
+      float G = quad_gmax<GD>(sg + o, bad);
+      if (c.check_inf) ms.bad |= bad;
+      if (c.has_gscale) G = fabsf(scale_grad<GD>(G, c.gscale));
+      exact = quad_may_raise(c, lut, vbt, G, *reinterpret_cast<const uint2*>(sm + o),
+                             *reinterpret_cast<const uint2*>(sw + o), thr_m, thr_v);
+    }
+    if (exact) {
       float g[4];
       if constexpr (GD == LUMA_F32) {
         const float4 v = *reinterpret_cast<const float4*>(sg + o);
@@ -879,7 +969,7 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
           g[e] = (GD == LUMA_BF16) ? __uint_as_float(h[e] << 16)
                                    : __half2float(__ushort_as_half((unsigned short)h[e]));
       }
-      if (c.check_inf) ms.bad |= any_nonfinite(g);
+      if (c.check_inf && !qb) ms.bad |= any_nonfinite(g);
       scale_grads<GD>(c, g);
       const uint2 qm = *reinterpret_cast<const uint2*>(sm + o);
       const uint2 qw = *reinterpret_cast<const uint2*>(sw + o);
@@ -1600,6 +1690,7 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
     // 256 / c consecutive lanes of a bucket combine their maxima.
     const float* lut = nullptr;
     const float* vbt = nullptr;
+    bool qb = false;  // pass 1: quad bounds usable (quad_may_raise)
     if (lut_ok && !c.init && (o_hi - o_lo) * 8 >= kLutMinElems) {
       for (int i = threadIdx.x; i < kLutEntries; i += kThreads)
         s_lut[i] = expm1f(__fmul_rn((float)i, c.o_dm));
@@ -1619,6 +1710,35 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
       }
       __syncthreads();
       lut = s_lut;
+      if (!PASS2) {
+        // Quad bounds need vbt non-increasing and lut non-decreasing.  vbt
+        // becomes its suffix maxima (still >= v(q) of every code of a bucket;
+        // v(q) falls with q, so this loosens it little), warp 0, eight entries
+        // per lane.  lut, the exact decode table, is only checked: one
+        // inversion (not seen, the entries are spaced by a factor >= e^dm)
+        // or a NaN entry turns the quad bounds off for the segment.
+        if (threadIdx.x < 32) {
+          uint32_t e[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) e[k] = __float_as_uint(s_vbound[threadIdx.x * 8 + k]);
+#pragma unroll
+          for (int k = 6; k >= 0; --k) e[k] = max(e[k], e[k + 1]);
+          uint32_t sfx = e[0];  // suffix maximum over lanes >= this one
+#pragma unroll
+          for (int k = 1; k < 32; k <<= 1) {
+            const uint32_t t = __shfl_down_sync(0xffffffffu, sfx, k);
+            if (threadIdx.x + k < 32) sfx = max(sfx, t);
+          }
+          uint32_t nxt = __shfl_down_sync(0xffffffffu, sfx, 1);
+          if (threadIdx.x == 31) nxt = 0u;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) s_vbound[threadIdx.x * 8 + k] = __uint_as_float(max(e[k], nxt));
+        }
+        int inv = 0;
+        for (int i = threadIdx.x; i < kLutEntries - 1; i += kThreads)
+          inv |= !(s_lut[i] <= s_lut[i + 1]);
+        qb = __syncthreads_or(inv) == 0;  // also publishes the suffix maxima
+      }
     }
 
     if (!PASS2) {
@@ -1631,9 +1751,9 @@ luma_pass_kernel(const LumaStepArgs a, const int lut_ok, PassAccum* acc) {
         const int64_t o_full = min(o_hi, d.numel / 8);
         if (o_full > o_lo) {
           switch (d.grad_dtype) {
-            case LUMA_F32: pass1_staged<LUMA_F32>(d, c, lut, vbt, 2 * o_lo, 2 * o_full, ms); break;
-            case LUMA_BF16: pass1_staged<LUMA_BF16>(d, c, lut, vbt, 2 * o_lo, 2 * o_full, ms); break;
-            default: pass1_staged<LUMA_F16>(d, c, lut, vbt, 2 * o_lo, 2 * o_full, ms); break;
+            case LUMA_F32: pass1_staged<LUMA_F32>(d, c, lut, vbt, qb, 2 * o_lo, 2 * o_full, ms); break;
+            case LUMA_BF16: pass1_staged<LUMA_BF16>(d, c, lut, vbt, qb, 2 * o_lo, 2 * o_full, ms); break;
+            default: pass1_staged<LUMA_F16>(d, c, lut, vbt, qb, 2 * o_lo, 2 * o_full, ms); break;
           }
           ob = o_full;
         }

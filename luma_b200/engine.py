@@ -23,6 +23,7 @@ its step, row and seed without host work.
 from __future__ import annotations
 
 import ctypes
+import itertools
 from dataclasses import dataclass
 
 import numpy as np
@@ -101,6 +102,59 @@ def build_desc_table(segs: list[Segment]) -> tuple[np.ndarray, int]:
     return d, int(octs.sum())
 
 
+class Columns:
+    """The descriptor table of a plain step as columns (no multicast, no
+    injected draws, counters from 0): the optimizer's per-step fast path.
+
+    ``statics[i]`` is a tuple ``(param_ptr, q_m_ptr, q_w_ptr, numel, param_id,
+    slot, param_dtype_code)`` that the caller keeps per parameter and reuses
+    step after step (so comparing two signatures mostly compares identical
+    objects); ``grad_ptrs``, ``grad_codes`` and ``rows`` change per step."""
+
+    __slots__ = ("statics", "grad_ptrs", "grad_codes", "rows")
+
+    def __init__(self):
+        self.statics: list[tuple] = []
+        self.grad_ptrs: list[int] = []
+        self.grad_codes: list[int] = []
+        self.rows: list[int] = []
+
+    def __len__(self) -> int:
+        return len(self.statics)
+
+    def signature(self) -> tuple:
+        return (tuple(self.statics), tuple(self.grad_ptrs), tuple(self.grad_codes),
+                tuple(self.rows))
+
+
+def build_desc_table_columns(cols: Columns) -> tuple[np.ndarray, int]:
+    """numpy LumaTensorDesc table and total octet count of a ``Columns`` (the
+    same table ``build_desc_table`` makes for the equivalent segments)."""
+    n = len(cols)
+    d = np.zeros(n, dtype=DESC_DTYPE)
+    if n == 0:
+        return d, 0
+    st = np.fromiter(itertools.chain.from_iterable(cols.statics), dtype=np.int64,
+                     count=7 * n).reshape(n, 7)
+    grad = np.array(cols.grad_ptrs, dtype=np.uint64)
+    d["param"] = st[:, 0]
+    d["grad"] = grad
+    d["q_m"] = st[:, 1]
+    d["q_w"] = st[:, 2]
+    numel = st[:, 3]
+    octs = (numel + 7) // 8
+    d["numel"] = numel
+    d["oct_begin"] = np.concatenate([np.zeros(1, np.int64), np.cumsum(octs)[:-1]])
+    d["param_id"] = st[:, 4]
+    d["row"] = np.array(cols.rows, dtype=np.int32)
+    d["slot"] = st[:, 5]
+    d["param_dtype"] = st[:, 6]
+    d["grad_dtype"] = np.array(cols.grad_codes, dtype=np.uint8)
+    d["vec_ok"] = ((st[:, 0] % 16 == 0) & (st[:, 1] % 16 == 0) & (st[:, 2] % 16 == 0)
+                   & (grad % 16 == 0)).astype(np.uint8)
+    return d, int(octs.sum())
+
+
 class DeviceEngine:
     def __init__(self, device: torch.device):
         self.device = device
@@ -115,6 +169,7 @@ class DeviceEngine:
         self._n_desc = 0
         self._total_oct = 0
         self._tables: dict[tuple, tuple[torch.Tensor, int, int]] = {}  # sig -> (descs, n, octets)
+        self._pinned_tables: list[tuple[torch.Tensor, torch.cuda.Event]] = []  # copies in flight
         self._args = _lib.LumaStepArgs()
 
     # -- slots ---------------------------------------------------------------
@@ -167,7 +222,22 @@ class DeviceEngine:
             self.rows_dev[:nbytes].copy_(buf[:nbytes], non_blocking=True)
             ev.record(stream)
 
-    def step(self, segs: list[Segment], rows: np.ndarray | None, base_seed: int,
+    def _upload_table(self, table: np.ndarray, stream: torch.cuda.Stream) -> torch.Tensor:
+        """Device copy of a descriptor table, stream-ordered from pinned host
+        memory (a pageable copy would wait for the kernels still running)."""
+        host = torch.from_numpy(table.view(np.uint8)).pin_memory()
+        dev = torch.empty(host.numel(), dtype=torch.uint8, device=self.device)
+        with torch.cuda.stream(stream):
+            dev.copy_(host, non_blocking=True)
+        # the pinned buffer is kept until the copy recorded on `stream` has run
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._pinned_tables.append((host, ev))
+        while self._pinned_tables and self._pinned_tables[0][1].query():
+            self._pinned_tables.pop(0)
+        return dev
+
+    def step(self, segs: "list[Segment] | Columns", rows: np.ndarray | None, base_seed: int,
              stream: torch.cuda.Stream | None = None, events=None, max_ctas: int = 0,
              row_table: torch.Tensor | None = None,
              grad_scale: torch.Tensor | None = None,
@@ -179,11 +249,16 @@ class DeviceEngine:
         by (in the grad's dtype) inside the kernels.  `found_inf`: optional
         float32 device flag pass 1 raises on an inf/NaN grad; when set, pass 2
         leaves every param, code and step count unchanged."""
-        if not segs:
+        if not len(segs):
             return
         if stream is None:
             stream = torch.cuda.current_stream(self.device)
-        sig = tuple(s.key() for s in segs)
+        if isinstance(segs, Columns):
+            sig = segs.signature()
+            build = build_desc_table_columns
+        else:
+            sig = tuple(s.key() for s in segs)
+            build = build_desc_table
         if sig != self._sig:
             # A few recent tables are kept, so callers that alternate grad
             # buffers (double buffering) do not rebuild one every step.
@@ -192,9 +267,8 @@ class DeviceEngine:
                 if torch.cuda.is_current_stream_capturing():
                     raise RuntimeError("LUMA: the set of parameters with gradients changed while "
                                        "a CUDA graph was being captured")
-                table, total = build_desc_table(segs)
-                hit = (torch.from_numpy(table.view(np.uint8).copy()).to(self.device), len(segs),
-                       total)
+                table, total = build(segs)
+                hit = (self._upload_table(table, stream), len(segs), total)
                 if len(self._tables) >= _TABLE_CACHE:
                     self._tables.pop(next(iter(self._tables)))
                 self._tables[sig] = hit

@@ -24,13 +24,31 @@ import torch
 from torch.optim import Optimizer
 
 from . import _lib
-from .engine import DeviceEngine, Segment
+from .engine import Columns, DeviceEngine, Segment
 from .hostmath import SCALE_FLOOR_M, grid_record, precompute, rows_array, step_row, step_rows
 
 _BACKENDS = {"auto", "cuda", "triton"}
-_PARAM_DTYPES = (torch.float32, torch.bfloat16)
-_GRAD_DTYPES = (torch.float32, torch.bfloat16, torch.float16)
 _PLAIN_TENSOR_TYPES = (torch.Tensor, torch.nn.Parameter)
+_GRAD_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+_PARAM_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+def _ParamEntry(p, param: torch.Tensor) -> list:
+    """What holds for a parameter while its storage, size and dtype stay (one
+    address is never on two devices): [p, param, data_ptr, numel, dtype,
+    device index, shape, dtype code, state dict (set by the first step that
+    uses the entry), descriptor tuple or None].  Raises for a param the step
+    cannot take."""
+    numel = param.numel()
+    if numel:
+        if param.dtype not in _PARAM_CODE:
+            raise ValueError(
+                f"LUMA requires float32 or bfloat16 parameters (got {param.dtype}).")
+        if not param.is_cuda:
+            raise RuntimeError(
+                f"LUMA backend 'cuda' requires CUDA tensors (param on {param.device}).")
+    return [p, param, param.data_ptr(), numel, param.dtype, param.get_device(), param.shape,
+            _PARAM_CODE.get(param.dtype, -1), None, None]
 
 
 class LUMA(Optimizer):
@@ -101,6 +119,9 @@ class LUMA(Optimizer):
         self.capture_steps = int(capture_steps)
         self._row_tables: dict[torch.device, tuple[tuple, torch.Tensor]] = {}
         self._scale_refs: dict[torch.device, torch.Tensor] = {}
+        self._pcache: list = []  # per param position: _ParamEntry, while valid
+        self._state_ref = self.state
+        self._state_len = 0
 
     # ------------------------------------------------------------------
     # helpers
@@ -464,73 +485,109 @@ class LUMA(Optimizer):
                 loss = closure()
 
         # Pass A: validate everything before touching any state.  This loop
-        # and the next run once per tensor every step, so they avoid per-tensor
-        # torch calls that allocate (views, device objects): with 10,000
-        # tensors every microsecond per tensor is 10 ms per step.
+        # and the next run once per tensor every step (with 10,000 tensors
+        # every microsecond per tensor is 10 ms per step), so what stays valid
+        # while a param keeps its storage, size and dtype (its device, shape,
+        # dtype checks and its state dict) is kept per param position in
+        # self._pcache, and tensors are not used as dict keys (their hash is a
+        # Python call).
+        if self.state is not self._state_ref or len(self.state) != self._state_len:
+            self._pcache = []  # state replaced, cleared or grown from outside step()
+            self._state_ref = self.state
+        pcache = self._pcache
         work = []
-        param_idx = 0
+        idx = -1
         plain = _PLAIN_TENSOR_TYPES
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
-                param_idx += 1
+                idx += 1
                 grad = p.grad
                 if grad is None:
                     continue
                 param = p if type(p) in plain else self._unwrap_tensor(p)
                 if type(grad) not in plain:
                     grad = self._unwrap_tensor(grad)
-                if param.numel() == 0:
-                    continue  # empty FSDP shard on this rank
-                if grad.is_sparse:
+                if idx >= len(pcache):
+                    pcache.extend([None] * (idx + 1 - len(pcache)))
+                if grad.is_sparse and param.numel():
                     raise RuntimeError("LUMA does not support sparse gradients")
-                if param.dtype not in _PARAM_DTYPES:
-                    raise ValueError(
-                        f"LUMA requires float32 or bfloat16 parameters (got {param.dtype}).")
-                if grad.dtype not in _GRAD_DTYPES:
-                    raise ValueError(f"LUMA requires float32/bfloat16/float16 gradients "
-                                     f"(got {grad.dtype}).")
-                if not param.is_cuda:
-                    raise RuntimeError(
-                        f"LUMA backend 'cuda' requires CUDA tensors (param on {param.device}).")
-                dev = param.get_device()
-                if grad.get_device() != dev:
-                    raise ValueError("LUMA requires the gradient on the parameter's device")
-                if grad.shape != param.shape:
-                    raise ValueError("LUMA requires the gradient to have the parameter's shape")
+                e = pcache[idx]
+                if e is None or e[0] is not p or e[1] is not param or e[2] != param.data_ptr() \
+                        or e[3] != param.numel() or e[4] is not param.dtype:
+                    e = pcache[idx] = _ParamEntry(p, param)
+                if e[3] == 0:
+                    continue  # empty FSDP shard on this rank
                 if not param.is_contiguous():
                     raise ValueError("LUMA CUDA kernel requires contiguous parameters")
+                gcode = _GRAD_CODE.get(grad.dtype)
+                if gcode is None:
+                    raise ValueError(f"LUMA requires float32/bfloat16/float16 gradients "
+                                     f"(got {grad.dtype}).")
+                if grad.get_device() != e[5]:
+                    raise ValueError("LUMA requires the gradient on the parameter's device")
+                if grad.shape != e[6]:
+                    raise ValueError("LUMA requires the gradient to have the parameter's shape")
                 if not grad.is_contiguous():
                     raise ValueError("LUMA CUDA kernel requires contiguous gradients")
-                work.append((p, param, grad, gi, param_idx - 1, dev))
+                work.append((e, grad, gi, idx, gcode))
 
-        # Pass B: state bookkeeping and per-device segment lists.
-        per_idx: dict[int, tuple[list[Segment], dict]] = {}
-        for p, param, grad, gi, pidx, dev in work:
-            state = self.state[p]
-            if "step" not in state:
-                state["step"] = 0
-                state["param_id"] = pidx
-            state["step"] += 1
-            t = state["step"]
+        # Pass B: state bookkeeping and the per-device descriptor columns (or
+        # segments, when the draw hook supplies per-tensor uniforms).
+        hook = self._draw_hook
+        if hook is not None and self.capturable:
+            raise RuntimeError("the draw hook is not available in capturable mode")
+        per_idx: dict[int, tuple] = {}
+        last_dev, cols, rowmap = None, None, None
+        last_gt, last_row = None, 0
+        for e, grad, gi, pidx, gcode in work:
+            param, state = e[1], e[8]
+            if state is None:
+                state = e[8] = self.state[e[0]]
+            t = state.get("step", 0) + 1
             if t == 1:
+                state["param_id"] = pidx
                 state["Q_m"] = torch.empty_like(param, dtype=torch.int16)
                 state["Q_w"] = torch.empty_like(param, dtype=torch.int16)
-            if "_slot" not in state:
-                state["_slot"] = self._new_slot(param.device)
-            segs, rowmap = per_idx.setdefault(dev, ([], {}))
+            state["step"] = t
+            slot = state.get("_slot")
+            if slot is None:
+                slot = state["_slot"] = self._new_slot(param.device)
+            if e[5] != last_dev:
+                last_dev, last_gt = e[5], None
+                entry = per_idx.get(last_dev)
+                if entry is None:
+                    entry = per_idx[last_dev] = ([] if hook is not None else Columns(), {})
+                cols, rowmap = entry
             if self.capturable:
                 row = gi * self.capture_steps  # the group's block of the row table
+            elif last_gt is not None and last_gt[0] == gi and last_gt[1] == t:
+                row = last_row
             else:
-                row = rowmap.setdefault((gi, t), len(rowmap))
-            seg = Segment(param, grad, state["Q_m"], state["Q_w"], state["param_id"], row,
-                          state["_slot"])
-            if self._draw_hook is not None:
-                if self.capturable:
-                    raise RuntimeError("the draw hook is not available in capturable mode")
-                um, uw = self._draw_hook(state["param_id"], t, param)
+                last_gt = (gi, t)
+                row = rowmap.get(last_gt)
+                if row is None:
+                    row = rowmap[last_gt] = len(rowmap)
+                last_row = row
+            q_m = state["Q_m"]
+            if hook is not None:
+                seg = Segment(param, grad, q_m, state["Q_w"], state["param_id"], row, slot)
+                um, uw = hook(state["param_id"], t, param)
                 seg.u_m = um.reshape(-1)
                 seg.u_w = uw.reshape(-1)
-            segs.append(seg)
+                cols.append(seg)
+                continue
+            # (param address, codes, param_id, slot) change rarely: one tuple
+            # per param, rebuilt when one of them did
+            sk = e[9]
+            if sk is None or sk[0] is not q_m or sk[1] != state["param_id"] or sk[2] != slot:
+                sk = e[9] = (q_m, state["param_id"], slot,
+                             (e[2], q_m.data_ptr(), state["Q_w"].data_ptr(), e[3],
+                              state["param_id"], slot, e[7]))
+            cols.statics.append(sk[3])
+            cols.grad_ptrs.append(grad.data_ptr())
+            cols.grad_codes.append(gcode)
+            cols.rows.append(row)
+        self._state_len = len(self.state)
 
         per_dev = {torch.device("cuda", k): v for k, v in per_idx.items()}
         if found_inf is not None:
@@ -564,8 +621,8 @@ class LUMA(Optimizer):
         """A step the kernels skipped (inf/NaN grads): restore the per-param
         step counts; a param whose first step was skipped gets no state, as if
         ``step()`` had not been called (its slot is kept for the next try)."""
-        for p, *_ in work:
-            state = self.state[p]
+        for e, *_ in work:
+            state = e[8]
             state["step"] -= 1
             if state["step"] == 0:
                 for key in ("step", "param_id", "Q_m", "Q_w"):

@@ -148,6 +148,34 @@ class TestStepping:
         with pytest.raises(ValueError, match="contiguous gradients"):
             opt.step()
 
+    def test_param_storage_or_layout_changed_between_steps(self):
+        """The step keeps per-param checks while a param keeps its storage,
+        size and dtype; a param whose data is replaced (new storage), made
+        non-contiguous, or whose grads switch dtype between steps is handled
+        as on the first step: same results as an optimizer that never saw
+        the old tensors, or the same error."""
+        seed_all(7)
+        a = nn.Parameter(torch.randn(3000, device=DEV) * 0.02)
+        b = nn.Parameter(a.detach().clone())
+        opt_a, opt_b = LUMA([a], lr=1e-3), LUMA([b], lr=1e-3)
+        opt_b._base_seed = opt_a._base_seed
+        a.grad_dtype = None  # the last step's grads are bf16
+        b.grad_dtype = None
+        grads = [torch.randn(3000, device=DEV) * 1e-3 for _ in range(4)]
+        for k, g in enumerate(grads):
+            if k == 2:
+                a.data = a.data.clone()  # new storage under the same Parameter
+            a.grad = g.clone() if k != 3 else g.to(torch.bfloat16)
+            b.grad = g.clone() if k != 3 else g.to(torch.bfloat16)
+            opt_a.step()
+            opt_b.step()
+            assert torch.equal(a, b), f"step {k + 1}"
+        assert torch.equal(opt_a.state[a]["Q_m"], opt_b.state[b]["Q_m"])
+        a.data = a.data.view(60, 50).t()  # same storage and size, not contiguous
+        a.grad = torch.zeros(50, 60, device=DEV)
+        with pytest.raises(ValueError, match="contiguous parameters"):
+            opt_a.step()
+
     def test_bf16_params_and_autocast_grads(self):
         m = nn.Linear(32, 16).to(DEV).to(torch.bfloat16)
         opt = LUMA(m.parameters(), lr=1e-2)

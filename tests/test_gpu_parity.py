@@ -336,6 +336,21 @@ def _crafted_grads(step, n, kind, gen):
         return base
     if kind == "flip":
         return torch.full((n,), 1e-2 * (-1.0) ** step) + base * 1e-4
+    if kind == "quad_spikes":
+        # maxima at every offset within a 4-element quad, both signs; at step
+        # 4 the largest v' (an earlier spike's, decaying slowly) and the
+        # largest |m'| (a new, smaller spike) sit in different elements
+        a = 4 * (n // 12) + 2                       # offset 2
+        if step == 1:
+            base[4 * (n // 20)] = 1.5               # offset 0
+        if step == 2:
+            base[a] = 3.0
+        if step >= 3:
+            base[a] = 0.0
+            base[a + 4 * 1009 + 1] = -0.37 * step   # offset 3
+        if step == 4:
+            base[a + 4 * 1009 - 1] = -2.6           # offset 1
+        return base
     raise ValueError(kind)
 
 
@@ -362,6 +377,35 @@ def test_scale_max_adversarial_bit_exact(beta1):
         orc.step()
         for i, (a, b) in enumerate(zip(pk, po)):
             assert torch.equal(a, b), f"step {step} tensor {i} ({kinds[i % len(kinds)]})"
+        _assert_same_state(f"step {step}", opt, orc, pk, po, [{"params": pk}])
+
+
+@pytest.mark.parametrize("gdt", [torch.bfloat16, torch.float32])
+def test_scale_max_adversarial_long_segments_bit_exact(gdt):
+    """The crafted grads on tensors long enough for the decode and bucket
+    tables on every CTA, where pass 1 bounds |m'| and v' once per quad of 4
+    elements and skips quads that cannot raise the maxima: ties (bound equal
+    to the running maximum), all-zero and subnormal grads, spikes at every
+    offset within a quad, a maximum of v' apart from the maximum of |m'|."""
+    LUMA = _luma()
+    kinds = ["ulp_ties", "zeros", "subnormal", "quad_spikes"]
+    n = 20_000_011
+    gen = torch.Generator().manual_seed(5)
+    pk = [(torch.randn(n, generator=gen) * 0.02).to(DEV) for _ in kinds]
+    po = [t.clone() for t in pk]
+    for t in pk + po:
+        t.grad_dtype = None
+    opt = LUMA(pk, lr=1e-3)
+    orc = OracleLUMA(po, lr=1e-3, draws=_philox_draws(opt))
+    for step in range(1, 5):
+        for k, kind in enumerate(kinds):
+            g = _crafted_grads(step, n, kind, gen).to(gdt).to(DEV)
+            pk[k].grad = g.clone()
+            po[k].grad = g.clone()
+        opt.step()
+        orc.step()
+        for i, (a, b) in enumerate(zip(pk, po)):
+            assert torch.equal(a, b), f"step {step} tensor {i} ({kinds[i]})"
         _assert_same_state(f"step {step}", opt, orc, pk, po, [{"params": pk}])
 
 

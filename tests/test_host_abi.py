@@ -141,6 +141,34 @@ def test_desc_table_octets_and_alignment():
     assert list(table["param_dtype"]) == [0] * 4 and list(table["slot"]) == [0, 1, 2, 3]
 
 
+def test_column_table_equals_segment_table():
+    """The optimizer's per-step fast path (descriptor columns) builds the same
+    bytes as the Segment path for the same tensors, dtypes, rows and slots."""
+    from luma_b200.engine import Columns, build_desc_table_columns, dtype_code
+    rng = np.random.default_rng(4)
+    buf = torch.zeros(1 << 16)
+    hb = torch.zeros(1 << 16, dtype=torch.bfloat16)
+    q = torch.zeros(1 << 17, dtype=torch.int16)
+    segs, cols = [], Columns()
+    off = 0
+    for k in range(40):
+        n = int(rng.integers(1, 600))
+        p = (buf if k % 2 else hb)[off:off + n]
+        g = (hb if k % 3 else buf)[off + 1:off + 1 + n] if k % 5 == 0 else (hb if k % 3 else buf)[off:off + n]
+        m, w = q[2 * off:2 * off + n], q[2 * off + n:2 * off + 2 * n]
+        row, slot = int(rng.integers(0, 3)), 39 - k
+        segs.append(Segment(p, g, m, w, param_id=k, row=row, slot=slot))
+        cols.statics.append((p.data_ptr(), m.data_ptr(), w.data_ptr(), n, k, slot,
+                             dtype_code(p.dtype)))
+        cols.grad_ptrs.append(g.data_ptr())
+        cols.grad_codes.append(dtype_code(g.dtype))
+        cols.rows.append(row)
+        off += n + int(rng.integers(0, 9))
+    t1, n1 = build_desc_table(segs)
+    t2, n2 = build_desc_table_columns(cols)
+    assert n1 == n2 and t1.tobytes() == t2.tobytes()
+
+
 def test_new_entry_points_reject_bad_arguments_without_gpu():
     h = _lib.lib()
     assert h.luma_error_flags(None, 0) == _lib.LUMA_ERR_INVALID
