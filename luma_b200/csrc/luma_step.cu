@@ -1514,13 +1514,16 @@ __device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, c
       if (rare) {
         pass2_pair_exact<PD, GD>(k0, k1, p_lo + ii);
       } else {
-        if (mcp != nullptr) {
-          mc_store2<PD>(mcp, 2 * (int64_t)ii, true, p0, p1);
-        } else if constexpr (PD == LUMA_F32) {
-          __stcs(pp + ii, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
-        } else {
-          __stcs(pp + ii, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
-                              ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p1)) << 16));
+        // the multicast mapping (replica: it includes this GPU's copy), and
+        // the param itself unless the mapping covers it
+        if (mcp != nullptr) mc_store2<PD>(mcp, 2 * (int64_t)ii, true, p0, p1);
+        if (mcp == nullptr || d.mc_local) {
+          if constexpr (PD == LUMA_F32) {
+            __stcs(pp + ii, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
+          } else {
+            __stcs(pp + ii, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
+                                ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p1)) << 16));
+          }
         }
         __stcs(qmp + ii, (qm0 & 0xFFFFu) | (qm1 << 16));
         __stcs(qwp + ii, (qw0 & 0xFFFFu) | (qw1 << 16));

@@ -355,7 +355,10 @@ class ZeroLUMA:
     elements, the grads' layout), and each bucket is all-gathered (NCCL) into
     one of ``staging`` rotating buffers of ``layout.span`` elements;
     ``consumer(bucket, view)``, called with the gather's stream current, gets
-    each gathered bucket before its buffer is reused.
+    each gathered bucket before its buffer is reused.  Positions of a view
+    outside every tensor (alignment gaps, the last bucket's padding) are not
+    data: NCCL gathers carry the shards' values there, the nvls staging mode
+    leaves them as they were.
     """
 
     def __init__(self, flat_param: torch.Tensor, layout: FlatLayout, rank: int,

@@ -22,6 +22,9 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
 
 SHAPES = [(4096, 64), (1000,), (3,), (256, 257), (70_001,), (64, 64), (5,)]
+# "+large": one more tensor long enough that every CTA runs the steady pass-2
+# loop on its shard, whose multicast stores then carry the gather
+LARGE = [(48_000_003,)]
 
 
 def _free_port():
@@ -46,13 +49,15 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
     msgs = []
     try:
         pdt = getattr(torch, pdt_name)
-        numels = [int(torch.tensor(s).prod()) if s else 1 for s in SHAPES]
+        shapes = SHAPES + (LARGE if gather.endswith("+large") else [])
+        gather = gather.removesuffix("+large")
+        numels = [int(torch.tensor(s).prod()) if s else 1 for s in shapes]
         lay = plan_layout(numels, world, buckets)
         gen = torch.Generator().manual_seed(5)
         flat = alloc_flat(lay.total, pdt, dev, gather if gather in ("nccl", "copy", "nvls")
                           else "nccl")
         flat.zero_()
-        for v, s in zip(flat_views(flat, lay, SHAPES), SHAPES):
+        for v, s in zip(flat_views(flat, lay, shapes), shapes):
             v.copy_((torch.randn(s, generator=gen) * 0.02).to(pdt))
         segs = shard_segments(lay, rank)
         sharded = gather.startswith("sharded")
@@ -118,10 +123,12 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
             if not torch.equal(other, rep):
                 msgs.append(f"t={t}: gathered replicas differ")
             if sharded:
-                for b in range(lay.buckets):
-                    lo, hi = lay.owned(rank, b)
-                    if not torch.equal(gathered[lo:hi], flat[b * lay.piece:(b + 1) * lay.piece]):
-                        msgs.append(f"t={t}: gathered bucket {b} lacks this rank's piece")
+                # every element of this rank's tensors is in the gathered
+                # buckets (positions outside every tensor are not data)
+                for k, sg in enumerate(segs):
+                    if not torch.equal(gathered[sg.flat:sg.flat + sg.length],
+                                       flat[sg.local:sg.local + sg.length]):
+                        msgs.append(f"t={t}: gathered bucket {sg.bucket} lacks segment {k}")
         opt.close()
         out_q.put((rank, msgs))
     except Exception as exc:  # noqa: BLE001
@@ -134,7 +141,8 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
     ("bfloat16", 1, "nccl"), ("float32", 1, "nccl"), ("bfloat16", 3, "nccl"),
     ("bfloat16", 3, "copy"), ("float32", 1, "copy"), ("bfloat16", 3, "sharded"),
     ("bfloat16", 3, "nvls"), ("float32", 1, "nvls"), ("bfloat16", 3, "sharded-nvls"),
-    ("float32", 2, "sharded-nvls")])
+    ("float32", 2, "sharded-nvls"), ("bfloat16", 1, "nvls+large"),
+    ("bfloat16", 1, "sharded-nvls+large")])
 def test_zero_sharded_step_two_gpus(pdt_name, buckets, gather):
     world = 2
     ctx = mp.get_context("spawn")
