@@ -553,15 +553,19 @@ def run_zero(args, rank, world, local_rank):
     if replica:
         opt.step(gshard)
         torch.cuda.synchronize()
-        words = flat.view(torch.int16 if flat.element_size() == 2 else torch.int32).to(torch.int64)
-        pos = torch.arange(words.numel(), device=device, dtype=torch.int64) % 65521 + 1
-        sig = torch.stack([words.sum(), (words * pos).sum()])
+        bits = flat.view(torch.int16 if flat.element_size() == 2 else torch.int32)
+        sig = torch.zeros(2, dtype=torch.int64, device=device)
+        chunk = 1 << 28  # widened to int64 a chunk at a time
+        for lo in range(0, bits.numel(), chunk):
+            words = bits[lo:lo + chunk].to(torch.int64)
+            pos = torch.arange(lo, lo + words.numel(), device=device, dtype=torch.int64) % 65521 + 1
+            sig += torch.stack([words.sum(), (words * pos).sum()])
+        del words, pos
         sigs = [torch.empty_like(sig) for _ in range(world)]
         dist.all_gather(sigs, sig)
         check = {"replicas_equal": all(torch.equal(sigs[0], x) for x in sigs),
                  "how": "after one more step: sum and position-weighted sum of every rank's "
                         "replica bits, all-gathered and compared"}
-        del words, pos
     opt.close()
     p1b, p2b = bytes_per_param(cfg["pdt"], cfg["gdt"])
     peak, peak_kind = measured_peak()
