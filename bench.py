@@ -844,7 +844,7 @@ def main():
         str(cfg["gdt"]).replace("torch.", "") + ", codes int16"
     config_out = {"workload": cfg["name"], "bytes_per_param": p1b + p2b,
                   "l2": "inputs larger than L2 (resident params+grads+codes >> 126 MB)"
-                  if args.config in ("llama8b", "ragged", "llama_layer") else "working set may fit L2",
+                  if args.config in ("llama8b", "llama70b", "ragged", "llama_layer") else "working set may fit L2",
                   "parallelism": (f"zero1-dp{world} (flat shards, per-shard scales, post-step "
                                   f"bf16 param all-gather)" if world > 1 else "single")}
 
