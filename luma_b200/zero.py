@@ -191,10 +191,11 @@ class NvlsGather:
 
 
 def auto_gather(world: int) -> str:
-    """Gather measured faster on B200 (Llama-3-8B, 8 buckets): copy engines up
-    to 4 ranks (2: 196 vs 145 Gparams/s, 4: 354 vs 212), NCCL at 8 (304 vs
-    291), where every rank receives 7/8 of the params and NCCL's transfer
-    rate (642 GB/s per rank) beats the copy engines' (580)."""
+    """Gather measured fastest on B200 (Llama-3-8B, 8 buckets): copy engines up
+    to 4 ranks (2 ranks: 207.5 Gparams/s against NVLS 178.1 and NCCL 158.9;
+    4 ranks: 354 against NCCL 212), NCCL at 8 (304-312 against copy engines
+    291 and NVLS 237), where every rank receives 7/8 of the params and NCCL's
+    transfer rate (643 GB/s per rank) beats the copy engines' (580)."""
     return "copy" if world <= 4 else "nccl"
 
 
