@@ -459,6 +459,31 @@ __device__ __forceinline__ bool logsr_up(float fr, float delta, float inv_z, flo
   return U < __fmul_rn(__fmul_rn(expm1f(x), inv_z), kUScale);
 }
 
+// The steady pass-2 loop evaluates the same series as one polynomial in the
+// fraction fr = y - floor(y) with the scalings folded into its coefficients:
+//   E = fr (c1 + fr (c2 + fr c3)),  c1 = d K, c2 = d^2 K / 2, c3 = d^3 K / 6,
+//   K = inv_z * 2^24 (d = fl32(delta), the factor of x = fl(fr * d)),
+// and takes diff = fl(U - E) in one FMA.  Against P = p* * 2^24 of the
+// reference expression: |P - S(x) K| <= 5 as above (the rounding of x moves
+// p* by at most 2^-24 relative, one more unit); the coefficients, rounded
+// from float64, and the three roundings of the evaluation add at most 6
+// relative ulps of E <= 2^24, i.e. 6; the final rounding at most 1.  So
+// |diff - (U - P)| <= 13 < 32 (the margin): whenever |diff| > 32 its sign is
+// the sign of U - P, the exact decision.
+// Where delta > kSeriesMaxDelta the coefficients are NaN instead, so that
+// every decision of the segment is undecided (|NaN| > margin is false) and the
+// margin of the steady loop is the constant kHotMargin.
+constexpr float kHotMargin = kDecisionMargin * kUScale;  // 32
+
+__device__ __forceinline__ void series_coefs(float d, float inv_z, float& c1, float& c2,
+                                             float& c3) {
+  const double k = (double)inv_z * (double)kUScale, x = (double)d;
+  const bool ok = d <= kSeriesMaxDelta;  // false for NaN
+  c1 = ok ? (float)(x * k) : __int_as_float(0x7FC00000);
+  c2 = (float)(x * x * k * 0.5);
+  c3 = (float)(x * x * x * k / 6.0);
+}
+
 // _quantize_momentum (functional.py:133-150) with _log_sr (functional.py:38-67).
 // |m.clamp(-S_m, S_m)| = min(|m|, S_m) (NaN kept); y >= 0 because log1pf of a
 // non-negative value is non-negative, so of clamp(0, K_M) only the upper bound
@@ -633,6 +658,9 @@ struct SegShared {
   int has_gscale;  // grads are scaled by gscale (LumaStepArgs.grad_scale)
   float gscale;
   int check_inf;   // pass 1 looks for inf / NaN grads (LumaStepArgs.found_inf)
+  // pass 2: the series of the steady loop's LogSR decisions folded into one
+  // polynomial in frac per code (series_coefs of the encode grid)
+  float pm1, pm2, pm3, pw1, pw2, pw3;
 };
 
 // The CTA's segment state and decode table.  At namespace scope so that the
@@ -1356,6 +1384,29 @@ __device__ __forceinline__ bool hot_segment(const SegShared& s) {
          s.enc.S_m <= kHotMaxM && s.enc.S_m <= kHotMaxQuot * eps && den_hi <= kHotMaxDen;
 }
 
+// Float to 16-bit integer conversions, truncating (the arguments are integral)
+// and saturating to the destination range (PTX cvt clamps float-to-integer
+// results); the result's 16 bits in the low half of a 32-bit word.
+__device__ __forceinline__ uint32_t f2u16_sat(float x) {
+  unsigned short h;
+  asm("cvt.rzi.u16.f32 %0, %1;" : "=h"(h) : "f"(x));
+  return (uint32_t)h;
+}
+
+__device__ __forceinline__ uint32_t f2i16_bits(float x) {
+  unsigned short h;
+  asm("cvt.rzi.s16.f32 %0, %1;" : "=h"(h) : "f"(x));
+  return (uint32_t)h;
+}
+
+// Two floats rounded to bf16 (RN) and packed, the first in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  uint32_t u;
+  memcpy(&u, &h, sizeof(u));
+  return u;
+}
+
 // pass2_elem for the steady state; sets `rare` when the element's results may
 // differ from pass2_elem's (they are then discarded).  Every value of an
 // element that is not marked is finite, so the NaN-keeping clamps of the
@@ -1383,25 +1434,25 @@ __device__ __forceinline__ void pass2_elem_hot(const Consts& c, const float* lut
     const float ac = fminf(a, c.n_sm32);
     const float y = __fmul_rn(log1pf(ac), c.n_inv_dm);
     const float fy = floorf(y);
-    const float x = __fmul_rn(__fsub_rn(y, fy), c.n_dm);
-    const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
-    const float diff = __fsub_rn(um, __fmul_rn(e, c.inv_zm24));
-    rare |= !(fabsf(diff) > c.margin_m);
+    const float fr = __fsub_rn(y, fy);  // exact
+    const float diff =
+        __fmaf_rn(-fr, __fmaf_rn(fr, __fmaf_rn(fr, g_seg.pm3, g_seg.pm2), g_seg.pm1), um);
+    rare |= !(fabsf(diff) > kHotMargin);
+    // y >= 0, so r >= 0; the sign of m' goes onto r and the conversion is exact
     const float r = fminf(__fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f), (float)LUMA_K_M);
-    const int ri = (int)r;
-    qm = (uint32_t)(uint16_t)(int16_t)(mn < 0.0f ? -ri : ri);
+    qm = f2i16_bits(__uint_as_float(__float_as_uint(r) | (__float_as_uint(mn) & 0x80000000u)));
   }
   {  // quant_w
     const float sq = v_ok ? sqrt_cr(vn) : 0.0f;
     const float w = fminf(fmaxf(rcp_cr(__fadd_rn(sq, c.eps32)), c.n_wmin), c.w_max);
     const float y = __fmul_rn(logf(__fmul_rn(w, c.n_inv_wmin)), c.n_inv_dw);
     const float fy = floorf(y);
-    const float x = __fmul_rn(__fsub_rn(y, fy), c.n_dw);
-    const float e = __fmaf_rn(__fmul_rn(x, x), __fmaf_rn(x, 1.0f / 6.0f, 0.5f), x);
-    const float diff = __fsub_rn(uw, __fmul_rn(e, c.inv_zw24));
-    rare |= !(fabsf(diff) > c.margin_w);
-    const float r = fminf(fmaxf(__fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f), 0.0f), (float)LUMA_K_W);
-    qw = (uint32_t)(int)r;
+    const float fr = __fsub_rn(y, fy);  // exact
+    const float diff =
+        __fmaf_rn(-fr, __fmaf_rn(fr, __fmaf_rn(fr, g_seg.pw3, g_seg.pw2), g_seg.pw1), uw);
+    rare |= !(fabsf(diff) > kHotMargin);
+    // clamp(0, K_W = 65535) is the saturation of the conversion to u16
+    qw = f2u16_sat(__fadd_rn(fy, diff < 0.0f ? 1.0f : 0.0f));
   }
 }
 
@@ -1521,12 +1572,11 @@ __device__ __forceinline__ void pass2_hot(const SegShared& s, const Consts& c, c
           if constexpr (PD == LUMA_F32) {
             __stcs(pp + ii, make_uint2(__float_as_uint(p0), __float_as_uint(p1)));
           } else {
-            __stcs(pp + ii, (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p0)) |
-                                ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(p1)) << 16));
+            __stcs(pp + ii, pack_bf16x2(p0, p1));
           }
         }
-        __stcs(qmp + ii, (qm0 & 0xFFFFu) | (qm1 << 16));
-        __stcs(qwp + ii, (qw0 & 0xFFFFu) | (qw1 << 16));
+        __stcs(qmp + ii, __byte_perm(qm0, qm1, 0x5410));
+        __stcs(qwp + ii, __byte_perm(qw0, qw1, 0x5410));
       }
     }
   }
@@ -1643,7 +1693,11 @@ __device__ void load_segment(const LumaStepArgs& a, int di, bool pass2, SegShare
     // re-derives the decode grid from (S_m, S_v) with the current eps.
     if (s.dec.eps != s.row.eps) make_grid(s.dec.S_m, s.dec.S_v, s.row.eps, &s.dec);
   }
-  if (pass2) s.enc = slot->grid[t & 1];
+  if (pass2) {
+    s.enc = slot->grid[t & 1];
+    series_coefs(s.enc.dm, s.enc.inv_zm, s.pm1, s.pm2, s.pm3);
+    series_coefs(s.enc.dw, s.enc.inv_zw, s.pw1, s.pw2, s.pw3);
+  }
 }
 
 // kStaticAcc: pass-1 accumulators at acc[descriptor index] (luma_step_noalloc)
