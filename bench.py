@@ -472,7 +472,8 @@ def run_zero(args, rank, world, local_rank):
     max_ctas = max(1, sms - args.reserve_sms) if args.reserve_sms > 0 else 0
     opt = ZeroLUMA(flat, lay, rank, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                    base_seed=1234, max_ctas=max_ctas, gather=gather,
-                   copy_streams=args.copy_streams, replica=replica)
+                   copy_streams=args.copy_streams, replica=replica,
+                   copy_lockstep=args.copy_lockstep)
     for _ in range(max(args.warmup, 1)):
         opt.step(gshard)
     torch.cuda.synchronize()
@@ -815,9 +816,13 @@ def main():
     ap.add_argument("--buckets", type=int, default=8,
                     help="N>1: gather buckets (each bucket's gather overlaps the next's kernels)")
     ap.add_argument("--reserve-sms", type=int, default=0,
-                    help="N>1, NCCL gather: SMs left free for NCCL while a gather is in flight")
+                    help="N>1, NCCL gather (and copy gather in lockstep): SMs the step kernels "
+                         "leave free for NCCL kernels while a gather is in flight")
     ap.add_argument("--copy-streams", type=int, default=1,
                     help="N>1, copy gather: streams the peer pushes are spread over (0: one per peer)")
+    ap.add_argument("--copy-lockstep", action="store_true",
+                    help="N>2, copy gather on one stream: a barrier between a bucket's pushes, so "
+                         "every GPU receives from one peer at a time")
     ap.add_argument("--gather", default="auto", choices=["auto", "nccl", "copy", "nvls"],
                     help="N>1: post-step all-gather by NCCL, by copy-engine pushes over CUDA IPC, "
                          "or fused into pass 2 as NVLink multicast stores (nvls)")

@@ -245,7 +245,7 @@ class PeerGather:
     """
 
     def __init__(self, flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None,
-                 copy_streams: int = 1):
+                 copy_streams: int = 1, lockstep: bool = False):
         import torch.distributed as dist
 
         from . import _lib
@@ -290,7 +290,13 @@ class PeerGather:
         n_st = 1 + max(k for _, k in order)
         self.copy_streams = [torch.cuda.Stream(device=dev) for _ in range(n_st)]
         self.streams = {p: self.copy_streams[k] for p, k in order}
+        self.order = [p for p, _ in order]
+        # lockstep (one copy stream): a barrier between consecutive pushes of a
+        # bucket, so that in phase k every rank pushes to rank + k and every
+        # GPU receives from exactly one peer at a time
+        self.lockstep = bool(lockstep) and n_st == 1 and layout.world > 2
         self.token = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.phase_token = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def _barrier(self) -> None:
         import torch.distributed as dist
@@ -311,6 +317,15 @@ class PeerGather:
         nbytes = (hi - lo) * es
         for st in self.copy_streams:
             st.wait_event(ready)
+        if self.lockstep:
+            import torch.distributed as dist
+            st = self.copy_streams[0]
+            for k, p in enumerate(self.order):
+                if k:
+                    with torch.cuda.stream(st):
+                        dist.all_reduce(self.phase_token, group=self.pg)
+                self._lib.copy_async(self.peer_ptr[p] + lo * es, src, nbytes, st)
+            return
         for p, st in self.streams.items():
             self._lib.copy_async(self.peer_ptr[p] + lo * es, src, nbytes, st)
 
@@ -330,12 +345,12 @@ class PeerGather:
 
 
 def make_peer_gather(flat: torch.Tensor, layout: FlatLayout, rank: int, process_group=None,
-                     copy_streams: int = 1) -> PeerGather | None:
+                     copy_streams: int = 1, lockstep: bool = False) -> PeerGather | None:
     """A PeerGather, or None (with a warning, on every rank alike) when the
     buffer cannot be shared over CUDA IPC; the caller then gathers by NCCL."""
     import warnings
     try:
-        return PeerGather(flat, layout, rank, process_group, copy_streams)
+        return PeerGather(flat, layout, rank, process_group, copy_streams, lockstep)
     except PeerMapError as exc:
         warnings.warn(f"ZeroLUMA: copy-engine gather unavailable ({exc}); using NCCL instead",
                       RuntimeWarning, stacklevel=3)
@@ -360,6 +375,12 @@ class ZeroLUMA:
     outside every tensor (alignment gaps, the last bucket's padding) are not
     data: NCCL gathers carry the shards' values there, the nvls staging mode
     leaves them as they were.
+
+    ``copy_lockstep`` (copy gather, one copy stream, more than 2 ranks): a
+    barrier between the pushes of a bucket, so that in phase k every rank
+    pushes to rank + k and every GPU receives from one peer at a time; the
+    step kernels then run on ``max_ctas`` CTAs so the barriers' NCCL kernels
+    find free SMs.
     """
 
     def __init__(self, flat_param: torch.Tensor, layout: FlatLayout, rank: int,
@@ -367,7 +388,7 @@ class ZeroLUMA:
                  weight_decay: float = 0.01, base_seed: int | None = None,
                  process_group=None, max_ctas: int = 0, gather: str = "nccl",
                  copy_streams: int = 1, replica: bool = True, staging: int = 2,
-                 consumer=None):
+                 consumer=None, copy_lockstep: bool = False):
         want = layout.total if replica else layout.shard
         if flat_param.dim() != 1 or flat_param.numel() != want:
             raise ValueError(f"flat_param must be 1-D with {want} elements")
@@ -435,7 +456,8 @@ class ZeroLUMA:
                               RuntimeWarning, stacklevel=2)
                 gather = "copy"
         if gather == "copy" and layout.world > 1:
-            self.peers = make_peer_gather(flat_param, layout, rank, process_group, copy_streams)
+            self.peers = make_peer_gather(flat_param, layout, rank, process_group, copy_streams,
+                                          copy_lockstep)
             if self.peers is None:
                 gather = "nccl"
         self.gather_mode = gather
@@ -587,10 +609,13 @@ class ZeroLUMA:
             self.nvls.barrier()
             return
         if self.peers is not None:
-            # copy engines: bucket b's pushes overlap bucket b+1's kernels
+            # copy engines: bucket b's pushes overlap bucket b+1's kernels; in
+            # lockstep the barriers between pushes are NCCL kernels, which
+            # need SMs the step kernels leave free (max_ctas)
             self.peers.begin(main)
+            cap = self.max_ctas if self.peers.lockstep else 0
             for b in range(self.layout.buckets):
-                self._step_bucket(b, grad_shard, rows, 0, grad_scale)
+                self._step_bucket(b, grad_shard, rows, cap, grad_scale)
                 done = torch.cuda.Event()
                 done.record(main)
                 self.peers.push(b, done)
