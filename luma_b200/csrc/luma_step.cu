@@ -84,6 +84,11 @@ constexpr size_t kPass2SmemBytes = kLutPadBytes + kHotStages * kHotStageBytes;
 #define LUMA_P1_STAGES 2
 #endif
 constexpr int kP1Stages = LUMA_P1_STAGES;
+// Staged pass-1 loop: iterations between exchanges of the warp's bounds.
+#ifndef LUMA_P1_SYNC_EVERY
+#define LUMA_P1_SYNC_EVERY 8
+#endif
+constexpr int kP1SyncEvery = LUMA_P1_SYNC_EVERY;
 constexpr size_t kP1StageBytes = (size_t)kThreadsPass1 * 32;
 constexpr size_t kPass1SmemBytes = kLutPadBytes + kP1Stages * kP1StageBytes;
 
@@ -967,13 +972,17 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
 #pragma unroll
   for (int k = 0; k < kP1Stages - 1; ++k) issue(threadIdx.x + (int64_t)k * kThreads, k);
   int st = 0;
+  // Finite thresholds: the largest exact maxima known to this lane.  They
+  // are refreshed after an exact evaluation and after each exchange of the
+  // warp's bounds (every kP1SyncEvery iterations); a stale threshold is still
+  // the value of an element seen, so it only skips fewer quads.
+  float thr_m = fminf(fmaxf(__uint_as_float(ms.am), ms.Tm), FLT_MAX);
+  float thr_v = fminf(fmaxf(__uint_as_float(ms.av), ms.Tv), FLT_MAX);
+  int it = 0;
   for (int64_t jb = 0; jb < n; jb += kThreads) {
     const int64_t j = jb + threadIdx.x;
     issue(j + (int64_t)(kP1Stages - 1) * kThreads, st == 0 ? kP1Stages - 1 : st - 1);
     cp_async_wait<kP1Stages - 1>();  // quad j has landed
-    // finite thresholds: the largest exact maxima known to this lane
-    const float thr_m = fminf(fmaxf(__uint_as_float(ms.am), ms.Tm), FLT_MAX);
-    const float thr_v = fminf(fmaxf(__uint_as_float(ms.av), ms.Tv), FLT_MAX);
     const size_t o = (size_t)st * kP1StageBytes;
     bool exact = j < n;
     if (qb && exact) {  // one bound per quad; see quad_may_raise
@@ -1012,10 +1021,18 @@ __device__ __forceinline__ void pass1_staged(const LumaTensorDesc& d, const Cons
           pass1_elem(c, lut, vbt, g[e], (int)(int16_t)(uint16_t)wm, ww, ms);
         }
       }
+      thr_m = fminf(fmaxf(__uint_as_float(ms.am), ms.Tm), FLT_MAX);
+      thr_v = fminf(fmaxf(__uint_as_float(ms.av), ms.Tv), FLT_MAX);
     }
     st = st == kP1Stages - 1 ? 0 : st + 1;
-    ms.warp_sync_bounds();
+    if (++it == kP1SyncEvery) {  // the same iteration count on every lane
+      it = 0;
+      ms.warp_sync_bounds();
+      thr_m = fminf(fmaxf(__uint_as_float(ms.am), ms.Tm), FLT_MAX);
+      thr_v = fminf(fmaxf(__uint_as_float(ms.av), ms.Tv), FLT_MAX);
+    }
   }
+  ms.warp_sync_bounds();
   cp_async_wait<0>();  // no copy left in flight into the stages
 }
 
