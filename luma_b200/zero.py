@@ -212,6 +212,15 @@ def push_order(rank: int, world: int, copy_streams: int) -> list[tuple[int, int]
     return [(p, k % n_st) for k, p in enumerate(peers)]
 
 
+def lockstep_applies(requested: bool, copy_streams: int, world: int) -> bool:
+    """Whether the copy gather runs in lockstep: a stream-ordered barrier
+    between consecutive pushes of a bucket, so that in phase k every rank
+    pushes to rank + k (``push_order``) and every GPU receives from exactly one
+    peer at a time.  Only with one copy stream (the pushes are then ordered)
+    and more than two ranks (with two there is one push per bucket)."""
+    return bool(requested) and copy_streams == 1 and world > 2
+
+
 def gather_bucket_into(staging: torch.Tensor, shard: torch.Tensor, layout: FlatLayout,
                        bucket: int, group=None) -> torch.Tensor:
     """Sharded-params mode: all-gather bucket `bucket` of every rank's shard
@@ -291,10 +300,7 @@ class PeerGather:
         self.copy_streams = [torch.cuda.Stream(device=dev) for _ in range(n_st)]
         self.streams = {p: self.copy_streams[k] for p, k in order}
         self.order = [p for p, _ in order]
-        # lockstep (one copy stream): a barrier between consecutive pushes of a
-        # bucket, so that in phase k every rank pushes to rank + k and every
-        # GPU receives from exactly one peer at a time
-        self.lockstep = bool(lockstep) and n_st == 1 and layout.world > 2
+        self.lockstep = lockstep_applies(lockstep, n_st, layout.world)
         self.token = torch.zeros(1, dtype=torch.float32, device=dev)
         self.phase_token = torch.zeros(1, dtype=torch.float32, device=dev)
 

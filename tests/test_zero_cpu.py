@@ -193,6 +193,18 @@ def test_push_order_rotates_and_covers_peers(world, streams):
         assert len({push_order(r, world, streams)[pos][0] for r in range(world)}) == world
 
 
+def test_lockstep_applies_only_to_one_ordered_stream_beyond_two_ranks():
+    from luma_b200.zero import lockstep_applies, push_order
+    assert lockstep_applies(True, 1, 8) and lockstep_applies(True, 1, 3)
+    assert not lockstep_applies(False, 1, 8)
+    assert not lockstep_applies(True, 2, 8)   # pushes on two streams are not ordered
+    assert not lockstep_applies(True, 1, 2)   # one push per bucket: nothing to separate
+    # in lockstep, phase k of every rank targets a distinct peer (a permutation)
+    for world in (3, 4, 8):
+        for k in range(world - 1):
+            assert len({push_order(r, world, 1)[k][0] for r in range(world)}) == world
+
+
 def _peer_fallback_worker(rank, world, port, out_q):
     import warnings
     os.environ["MASTER_ADDR"] = "127.0.0.1"
