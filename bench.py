@@ -462,7 +462,10 @@ def run_zero(args, rank, world, local_rank):
     buckets = args.buckets if replica else max(args.buckets, 32)
     lay = plan_layout(numels, world, buckets)
     gen = torch.Generator(device=device).manual_seed(0)
-    gather = auto_gather(world) if args.gather == "auto" else args.gather
+    if args.gather == "auto":
+        gather = auto_gather(world) if replica else "nccl"  # as ZeroLUMA resolves it
+    else:
+        gather = args.gather
     flat = alloc_flat(lay.total if replica else lay.shard, cfg["pdt"], device,
                       gather if replica else "nccl")
     flat.normal_(0.0, 0.02, generator=gen)

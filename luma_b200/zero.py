@@ -317,10 +317,17 @@ class PeerGather:
             st.wait_stream(self.comm)
 
     def push(self, bucket: int, ready: torch.cuda.Event) -> None:
+        """This rank's piece of bucket `bucket` into the same place of every
+        peer's buffer."""
         lo, hi = self.layout.owned(self.rank, bucket)
         es = self.flat.element_size()
-        src = self.flat.data_ptr() + lo * es
-        nbytes = (hi - lo) * es
+        self.push_range(self.flat.data_ptr() + lo * es, lo * es, (hi - lo) * es, ready)
+
+    def push_range(self, src: int, dst_off: int, nbytes: int, ready: torch.cuda.Event,
+                   local: bool = False) -> None:
+        """`nbytes` at device address `src` to byte offset `dst_off` of every
+        peer's buffer (and of this rank's own buffer when `local`), on the
+        copy streams after `ready`."""
         for st in self.copy_streams:
             st.wait_event(ready)
         if self.lockstep:
@@ -330,10 +337,13 @@ class PeerGather:
                 if k:
                     with torch.cuda.stream(st):
                         dist.all_reduce(self.phase_token, group=self.pg)
-                self._lib.copy_async(self.peer_ptr[p] + lo * es, src, nbytes, st)
-            return
-        for p, st in self.streams.items():
-            self._lib.copy_async(self.peer_ptr[p] + lo * es, src, nbytes, st)
+                self._lib.copy_async(self.peer_ptr[p] + dst_off, src, nbytes, st)
+        else:
+            for p, st in self.streams.items():
+                self._lib.copy_async(self.peer_ptr[p] + dst_off, src, nbytes, st)
+        if local:
+            self._lib.copy_async(self.flat.data_ptr() + dst_off, src, nbytes,
+                                 self.copy_streams[0])
 
     def finish(self, main: torch.cuda.Stream) -> None:
         """Barrier after every push; `main` then sees the full replica."""
@@ -374,13 +384,16 @@ class ZeroLUMA:
     ``replica=False`` is the mode for models whose full replica does not fit
     next to the shard state (Llama-3-70B on 8 GPUs: 141 GB of bf16 params):
     ``flat_param`` then holds only this rank's pieces (``layout.shard``
-    elements, the grads' layout), and each bucket is all-gathered (NCCL) into
-    one of ``staging`` rotating buffers of ``layout.span`` elements;
+    elements, the grads' layout), and each bucket is all-gathered (NCCL, or
+    with ``gather="copy"`` by copy-engine pushes into the peers' staging
+    buffers over CUDA IPC, or with ``gather="nvls"`` by the step's multicast
+    stores) into one of ``staging`` rotating buffers of ``layout.span`` elements;
     ``consumer(bucket, view)``, called with the gather's stream current, gets
     each gathered bucket before its buffer is reused.  Positions of a view
     outside every tensor (alignment gaps, the last bucket's padding) are not
-    data: NCCL gathers carry the shards' values there, the nvls staging mode
-    leaves them as they were.
+    data: NCCL and copy gathers carry the shards' values there, the nvls
+    staging mode leaves them as they were.  ``gather="auto"`` picks NCCL in
+    this mode.
 
     ``copy_lockstep`` (copy gather, one copy stream, more than 2 ranks): a
     barrier between the pushes of a bucket, so that in phase k every rank
@@ -426,17 +439,35 @@ class ZeroLUMA:
         if gather not in ("nccl", "copy", "auto", "nvls"):
             raise ValueError(f"gather must be 'nccl', 'copy', 'nvls' or 'auto', got {gather!r}")
         if gather == "auto":
-            gather = auto_gather(layout.world)
+            # sharded params: NCCL (measured at 4 and 8 ranks); replicas: by world size
+            gather = auto_gather(layout.world) if replica else "nccl"
         self.replica = replica
         self.consumer = consumer
         self.staging = []
         self.staging_mc = []
+        self.staging_peers = None
         self.peers = None
         self.nvls = None
+        self._token = torch.zeros(1, dtype=torch.float32, device=dev)
         if not replica:
             # the gathered buckets go to rotating staging buffers: filled by the
-            # step's own multicast stores (nvls) or by NCCL
-            gather = "nvls" if gather == "nvls" and layout.world > 1 else "nccl"
+            # step's own multicast stores (nvls), by copy-engine pushes into the
+            # peers' staging buffers (copy) or by NCCL
+            if layout.world == 1 or gather not in ("nvls", "copy"):
+                gather = "nccl"
+            if gather == "copy":
+                # one allocation for all staging buffers (one IPC mapping per
+                # peer); at least two, so a push never overwrites a bucket a
+                # peer's consumer may still read
+                n_st = max(staging, 2)
+                whole = torch.empty(n_st * layout.span, dtype=flat_param.dtype, device=dev)
+                self.staging_peers = make_peer_gather(whole, layout, rank, process_group, 1,
+                                                      copy_lockstep)
+                if self.staging_peers is None:
+                    gather = "nccl"
+                else:
+                    self.staging = [whole[k * layout.span:(k + 1) * layout.span]
+                                    for k in range(n_st)]
             if layout.world > 1 and gather == "nvls":
                 import warnings
                 try:
@@ -461,7 +492,7 @@ class ZeroLUMA:
                 warnings.warn(f"ZeroLUMA: {exc}; using the copy-engine gather instead",
                               RuntimeWarning, stacklevel=2)
                 gather = "copy"
-        if gather == "copy" and layout.world > 1:
+        if gather == "copy" and replica and layout.world > 1:
             self.peers = make_peer_gather(flat_param, layout, rank, process_group, copy_streams,
                                           copy_lockstep)
             if self.peers is None:
@@ -538,6 +569,42 @@ class ZeroLUMA:
         lo, hi = self.layout.owned(self.rank, b)
         dist.all_gather_into_tensor(self.flat[b * s:(b + 1) * s], self.flat[lo:hi], group=self.pg)
 
+    def _staged_pushes(self, main: torch.cuda.Stream, ready_of) -> None:
+        """Sharded-params mode with copy engines: for every bucket b, after the
+        event ``ready_of(b)`` (which may launch b's kernels), push this rank's
+        piece into every GPU's staging buffer b % S, this one's included; an
+        all-reduce of one element on the gather stream then says that every
+        piece of b has landed, and ``consumer(b, view)`` runs on that stream.
+        Bucket b's pushes wait for bucket b-1's barrier, which every rank
+        reaches only after its consumer(b-2): with S >= 2 buffers no push
+        overwrites a bucket a consumer may still read.  A barrier first says
+        that every rank is done with the last call's buckets."""
+        import torch.distributed as dist
+        sp, comm = self.staging_peers, self.comm
+        es = self.flat.element_size()
+        p, span, n_st = self.layout.piece, self.layout.span, len(self.staging)
+        copy = sp.copy_streams[0]
+        comm.wait_stream(main)
+        with torch.cuda.stream(comm):
+            dist.all_reduce(self._token, group=self.pg)
+        gate = torch.cuda.Event()
+        gate.record(comm)
+        for b in range(self.layout.buckets):
+            ready = ready_of(b)
+            copy.wait_event(gate)
+            sp.push_range(self.flat.data_ptr() + b * p * es,
+                          ((b % n_st) * span + self.rank * p) * es, p * es, ready, local=True)
+            pushed = torch.cuda.Event()
+            pushed.record(copy)
+            comm.wait_event(pushed)
+            with torch.cuda.stream(comm):
+                dist.all_reduce(self._token, group=self.pg)
+                gate = torch.cuda.Event()
+                gate.record(comm)
+                if self.consumer is not None:
+                    self.consumer(b, self.staging[b % n_st])
+        main.wait_stream(comm)
+
     @torch.no_grad()
     def step_local(self, grad_shard: torch.Tensor,
                    grad_scale: torch.Tensor | None = None) -> None:
@@ -574,6 +641,11 @@ class ZeroLUMA:
                 self.peers.push(b, done)
             self.peers.finish(main)
             return
+        if self.staging_peers is not None:
+            ready = torch.cuda.Event()
+            ready.record(main)
+            self._staged_pushes(main, lambda b: ready)
+            return
         if self.staging_mc:
             self.staging_mc[0].barrier()  # every rank is done with the last call's buckets
         for b in range(self.layout.buckets):
@@ -594,6 +666,16 @@ class ZeroLUMA:
                 self._step_bucket(b, grad_shard, rows, 0, grad_scale)
             return
         main = torch.cuda.current_stream(self.flat.device)
+        if self.staging_peers is not None:
+            cap = self.max_ctas if self.staging_peers.lockstep else 0
+
+            def kernels(b):
+                self._step_bucket(b, grad_shard, rows, cap, grad_scale)
+                done = torch.cuda.Event()
+                done.record(main)
+                return done
+            self._staged_pushes(main, kernels)
+            return
         if self.staging_mc:
             # bucket b's kernels write its pieces into every rank's staging
             # buffer b % S; the barrier after them says all pieces have landed
@@ -643,6 +725,9 @@ class ZeroLUMA:
         if self.peers is not None:
             self.peers.close()
             self.peers = None
+        if self.staging_peers is not None:
+            self.staging_peers.close()
+            self.staging_peers = None
         if self.nvls is not None:
             self.nvls.close()
             self.nvls = None

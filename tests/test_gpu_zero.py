@@ -4,8 +4,9 @@ Each rank steps its flat shard; every (tensor, shard) segment must equal the
 oracle (the reference's op sequence on CUDA) run on that segment alone with
 the backend's Philox stream (param_id = tensor index, counter offset = the
 segment's offset in the tensor).  After the all-gather (NCCL, or copy-engine
-pushes over CUDA IPC, or the step's own multicast stores through NVSwitch) both
-ranks must hold the same full parameter buffer,
+pushes over CUDA IPC, or the step's own multicast stores through NVSwitch; for
+the sharded-params mode into staging buffers) both ranks must hold the same
+full parameter buffer,
 and its pieces must be each owner's result.
 Skipped with fewer than 2 GPUs.
 """
@@ -70,7 +71,7 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
             def consumer(b, view):
                 gathered[b * lay.span:(b + 1) * lay.span].copy_(view)
 
-            mode = "nvls" if gather == "sharded-nvls" else "nccl"
+            mode = {"sharded-nvls": "nvls", "sharded-copy": "copy"}.get(gather, "nccl")
             opt = ZeroLUMA(flat, lay, rank, lr=1e-3, base_seed=1234567890123, replica=False,
                            consumer=consumer, gather=mode)
             if opt.gather_mode != mode:
@@ -142,7 +143,8 @@ def _worker(rank, world, port, pdt_name, buckets, gather, out_q):
     ("bfloat16", 3, "copy"), ("float32", 1, "copy"), ("bfloat16", 3, "sharded"),
     ("bfloat16", 3, "nvls"), ("float32", 1, "nvls"), ("bfloat16", 3, "sharded-nvls"),
     ("float32", 2, "sharded-nvls"), ("bfloat16", 1, "nvls+large"),
-    ("bfloat16", 1, "sharded-nvls+large")])
+    ("bfloat16", 1, "sharded-nvls+large"), ("bfloat16", 3, "sharded-copy"),
+    ("float32", 2, "sharded-copy")])
 def test_zero_sharded_step_two_gpus(pdt_name, buckets, gather):
     world = 2
     ctx = mp.get_context("spawn")
