@@ -860,11 +860,13 @@ def main():
         if rank != 0:
             return
         cb = cpu_baseline(args.config, args.steps, args.warmup, budget_s=60.0)
-        config_out["reference_params"] = "float32 (the reference rejects bf16 params)"
+        # the same config as this backend's line; the reference's own param
+        # dtype (it rejects bf16 params) is stated beside it
         line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "Gparams/s",
                 "n_gpus": args.gpus, "steps": cb["steps_timed"], "warmup": max(args.warmup, 2),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": dtype, "data": "synthetic", "config": config_out,
+                "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+                "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config_out,
+                "reference_params": "float32 (the reference rejects bf16 params)",
                 "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": "Gparams/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
